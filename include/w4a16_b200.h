@@ -1,0 +1,154 @@
+/*
+ * w4a16_b200.h — C ABI of the B200 (sm_100a) W4A16 GEMV library.
+ *
+ * Int4-weight x fp16-activation matrix-vector products with symmetric per-row or
+ * group-128 scales.  Every entry point takes plain device pointers, sizes and a
+ * CUDA stream, launches asynchronously on that stream, never synchronises (except
+ * w4a16_read_device_error), never throws, and returns a status code (enum
+ * w4a16_status).  Buffers are owned by the caller.
+ *
+ * The reference exposes its kernels as a pybind11 module compiled from
+ * kernels/w4a16_kernels.cu (bindings at kernels/w4a16_kernels.cu:189-195, host
+ * wrappers at :183-187, Python surface at src/w4a16/kernels.py:33-43).  Each
+ * "*_cuda" function below replaces the binding of the same name; where the
+ * reference allocated the output (kernels/w4a16_kernels.cu:183), the caller passes
+ * it here.
+ *
+ * Layouts (row-major, contiguous):
+ *   packed  uint8  [rows][cols/2]   int4 codes + 8, interleaved or simple packing
+ *                                   (src/w4a16/kernels.py:64-91)
+ *   scale   fp32 or fp16 [rows] (per-row) or [rows][cols/128] (group-128)
+ *   vec / x fp16   [cols] or [batch][cols]
+ *   out     fp32 (or fp16 via w4a16_gemv) [rows] or [batch][rows]
+ * Requirements: cols % 8 == 0 (cols % 128 == 0 for group-128), vec/x 16-byte
+ * aligned, packed 4-byte aligned, scale/out aligned to their element size.
+ * rows == 0 or batch == 0 is a no-op that returns W4A16_OK.
+ */
+#ifndef W4A16_B200_H
+#define W4A16_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st* w4a16_stream_t;
+
+enum w4a16_status {
+  W4A16_OK = 0,
+  W4A16_ERR_NULL = -1,      /* a required pointer is NULL */
+  W4A16_ERR_SHAPE = -2,     /* rows/cols/batch out of range, or cols not a multiple of 8 (128) */
+  W4A16_ERR_ALIGN = -3,     /* a pointer is not aligned as required */
+  W4A16_ERR_DTYPE = -4,     /* unknown dtype, packing or group code */
+  W4A16_ERR_WORKSPACE = -5, /* workspace smaller than w4a16_gemv_workspace_bytes() for a split */
+  W4A16_ERR_CUDA = -6,      /* a CUDA runtime call or kernel launch failed */
+  W4A16_ERR_KERNEL = -7     /* a kernel gave up on a bounded wait (w4a16_read_device_error) */
+};
+
+enum w4a16_dtype { W4A16_DTYPE_F32 = 0, W4A16_DTYPE_F16 = 1 };
+enum w4a16_packing { W4A16_PACK_INTERLEAVED = 0, W4A16_PACK_SIMPLE = 1 };
+
+/* ---------------------------------------------------------------------------
+ * Reference-mirroring entry points: out[r] = sum_k q[r][k] * scale * vec[k], fp32.
+ * ------------------------------------------------------------------------- */
+
+/* Replaces marlin_cuda (kernels/w4a16_kernels.cu:185,192 -> k_marlin :100-114;
+ * Python w4a16_gemv, src/w4a16/kernels.py:40). Interleaved packing, per-row scale. */
+int w4a16_marlin_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                      int rows, int cols, w4a16_stream_t stream);
+
+/* Replaces marlin_g128_cuda (kernels/w4a16_kernels.cu:185,192 -> k_marlin_g128 :121-138;
+ * Python w4a16_gemv_g128, src/w4a16/kernels.py:41). Interleaved packing, scale
+ * fp32 [rows][cols/128]. */
+int w4a16_marlin_g128_cuda(const uint8_t* packed, const float* scale, const void* vec,
+                           float* out, int rows, int cols, w4a16_stream_t stream);
+
+/* Replace the simple-packing ladder bindings byte_cuda, u32_cuda, u32_v4_cuda,
+ * champ_cuda and uint4_cuda (kernels/w4a16_kernels.cu:184-185,190-193 -> k_byte
+ * :50-56, k_u32 :59-69, k_u32_v4 :72-82, k_champ :85-96, k_uint4 :147-157; Python
+ * matvec_*, src/w4a16/kernels.py:33-37).  All five run the same sm_100a kernel on
+ * the simple packing, per-row fp32 scale, fp32 accumulation. */
+int w4a16_byte_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                    int rows, int cols, w4a16_stream_t stream);
+int w4a16_u32_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                   int rows, int cols, w4a16_stream_t stream);
+int w4a16_u32_v4_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                      int rows, int cols, w4a16_stream_t stream);
+int w4a16_champ_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                     int rows, int cols, w4a16_stream_t stream);
+int w4a16_uint4_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                     int rows, int cols, w4a16_stream_t stream);
+
+/* Replaces h2f32_cuda (kernels/w4a16_kernels.cu:185,194 -> k_h2f32 :161-171; Python
+ * matvec_h2f32, src/w4a16/kernels.py:38).  Deliberately lossy: the eight products of
+ * each packed word are multiplied and summed in fp16 before the fp32 accumulation.
+ * Simple packing, per-row fp32 scale. */
+int w4a16_h2f32_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                     int rows, int cols, w4a16_stream_t stream);
+
+/* Replaces fp16_cuda (kernels/w4a16_kernels.cu:187,194 -> k_fp16 :174-180; Python
+ * matvec_fp16, src/w4a16/kernels.py:43).  Dense fp16 mat [rows][cols] times fp16 vec,
+ * fp32 accumulation and output.  cols % 8 == 0, mat and vec 16-byte aligned. */
+int w4a16_fp16_cuda(const void* mat, const void* vec, float* out, int rows, int cols,
+                    w4a16_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * General entry point (superset of the bindings above).
+ * ------------------------------------------------------------------------- */
+
+/* out[b][r] = sum_k q[r][k] * scale(r, k) * x[b][k]  (+ bias[r]), b < batch.
+ * The kernels behind w4a16_marlin_cuda / w4a16_marlin_g128_cuda (and, with the
+ * simple packing, the ladder bindings) generalised to: fp16 or fp32 scales, a batch
+ * of up to any number of activation rows (tensor-core path handles 16 per pass), an
+ * fp16 or fp32 output, an optional fp32 bias (the epilogue W4A16Linear.forward
+ * applies at src/w4a16/kernels.py:122-124), and split-K for short-row layers.
+ *   group      0 (one scale per row) or 128 (one scale per 128 columns)
+ *   workspace  NULL, or a zero-filled device buffer of workspace_bytes; when at
+ *              least w4a16_gemv_workspace_bytes(batch, rows, cols) it enables the
+ *              split-K path for layers with few rows.  The kernels leave it zeroed.
+ *              Calls that share a workspace must be ordered on one stream. */
+int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_dtype, int group,
+               const void* x, int batch, int rows, int cols, void* out, int out_dtype,
+               const float* bias, void* workspace, size_t workspace_bytes,
+               w4a16_stream_t stream);
+
+/* Bytes of workspace that let w4a16_gemv use split-K for this problem size. */
+size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols);
+
+/* out[r][k] = fp16( fp32(q[r][k]) * fp32(scale(r, k)) ), fp16 [rows][cols], one
+ * round-to-nearest per step: bit-identical to (q.float() * scale_expanded).half()
+ * computed from the reference's dequant formula (src/w4a16/kernels.py:94-101). */
+int w4a16_dequant(const uint8_t* packed, int packing, const void* scale, int scale_dtype,
+                  int group, int rows, int cols, void* out, w4a16_stream_t stream);
+
+/* Quantise and pack on the GPU in one launch (the reference does this in torch on
+ * the host: quantize_int4_symmetric / quantize_int4_group, src/w4a16/kernels.py:47-60,
+ * then pack_int4 / pack_int4_interleaved, :64-91).  w is fp32 or fp16 [rows][cols];
+ * scale = max|w| / 7 per row (group 0) or per 128 columns (group 128), computed in
+ * fp32; q = clamp(round_half_even(w / scale), -8, 7); an all-zero row or group gets
+ * scale 0 and codes 0.  Codes and fp32 scales are bit-identical to the reference's
+ * for fp32 input.  packed uint8 [rows][cols/2]; scale fp32 or fp16. */
+int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int group, int packing,
+                        uint8_t* packed, void* scale, int scale_dtype, w4a16_stream_t stream);
+
+/* Reads and clears the error word that kernels set when a bounded wait runs out
+ * (0 = none).  Synchronises `stream`. */
+int w4a16_read_device_error(int* code, w4a16_stream_t stream);
+
+/* Static text for a status code. */
+const char* w4a16_status_string(int status);
+
+/* Detail of the last failure on the calling thread (empty if none). */
+const char* w4a16_last_error_string(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int w4a16_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W4A16_B200_H */

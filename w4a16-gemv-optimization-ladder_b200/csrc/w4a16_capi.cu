@@ -1,0 +1,229 @@
+// extern "C" entry points of libw4a16_b200.so (declared in include/w4a16_b200.h).
+// Host-side validation happens here, before anything is launched: a bad pointer,
+// shape, alignment or dtype code returns a status and launches nothing.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "w4a16_b200.h"
+#include "w4a16_internal.h"
+
+namespace {
+
+using w4a16::set_error;
+
+constexpr int kVersion = 1 * 10000 + 0 * 100 + 0;
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Shape / pointer checks shared by every GEMV-style entry point.
+int check_gemv(const void* packed, int packing, const void* scale, int scale_dtype, int group,
+               const void* x, int batch, int rows, int cols, const void* out, int out_dtype) {
+  if (packing != W4A16_PACK_INTERLEAVED && packing != W4A16_PACK_SIMPLE) {
+    set_error("unknown packing code %d", packing);
+    return W4A16_ERR_DTYPE;
+  }
+  if ((scale_dtype != W4A16_DTYPE_F32 && scale_dtype != W4A16_DTYPE_F16) ||
+      (out_dtype != W4A16_DTYPE_F32 && out_dtype != W4A16_DTYPE_F16)) {
+    set_error("unknown dtype code (scale %d, out %d)", scale_dtype, out_dtype);
+    return W4A16_ERR_DTYPE;
+  }
+  if (group != 0 && group != 128) {
+    set_error("group must be 0 (per-row) or 128, got %d", group);
+    return W4A16_ERR_DTYPE;
+  }
+  if (rows < 0 || cols <= 0 || batch < 0) {
+    set_error("bad shape rows=%d cols=%d batch=%d", rows, cols, batch);
+    return W4A16_ERR_SHAPE;
+  }
+  if (cols % 8 != 0 || (group && cols % group != 0)) {
+    set_error("cols=%d must be a multiple of %d", cols, group ? group : 8);
+    return W4A16_ERR_SHAPE;
+  }
+  if (rows == 0 || batch == 0) return W4A16_OK;
+  if (!packed || !scale || !x || !out) {
+    set_error("NULL pointer (packed %p, scale %p, x %p, out %p)", packed, scale, x, out);
+    return W4A16_ERR_NULL;
+  }
+  const size_t ssz = scale_dtype == W4A16_DTYPE_F32 ? 4 : 2;
+  const size_t osz = out_dtype == W4A16_DTYPE_F32 ? 4 : 2;
+  if (!aligned(packed, 4) || !aligned(x, 16) || !aligned(scale, ssz) || !aligned(out, osz)) {
+    set_error("misaligned pointer: packed needs 4 B, x 16 B, scale %zu B, out %zu B", ssz, osz);
+    return W4A16_ERR_ALIGN;
+  }
+  return W4A16_OK;
+}
+
+int gemv_common(const uint8_t* packed, int packing, const void* scale, int scale_dtype, int group,
+                const void* x, int batch, int rows, int cols, void* out, int out_dtype,
+                const float* bias, void* workspace, size_t workspace_bytes,
+                w4a16_stream_t stream) {
+  int rc = check_gemv(packed, packing, scale, scale_dtype, group, x, batch, rows, cols, out,
+                      out_dtype);
+  if (rc != W4A16_OK || rows == 0 || batch == 0) return rc;
+  if (bias && !aligned(bias, 4)) {
+    set_error("bias must be 4-byte aligned");
+    return W4A16_ERR_ALIGN;
+  }
+  w4a16::GemvProblem p;
+  p.packed = packed;
+  p.packing = packing;
+  p.scale = scale;
+  p.scale_dtype = scale_dtype;
+  p.group = group;
+  p.x = x;
+  p.M = batch;
+  p.N = rows;
+  p.K = cols;
+  p.y = out;
+  p.out_dtype = out_dtype;
+  p.bias = bias;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace ? workspace_bytes : 0;
+  p.split_k = 0;
+  p.stream = reinterpret_cast<cudaStream_t>(stream);
+  return w4a16::launch_gemv(p);
+}
+
+int ladder(const uint8_t* packed, const float* scale, const void* vec, float* out, int rows,
+           int cols, w4a16_stream_t stream) {
+  return gemv_common(packed, W4A16_PACK_SIMPLE, scale, W4A16_DTYPE_F32, 0, vec, 1, rows, cols, out,
+                     W4A16_DTYPE_F32, nullptr, nullptr, 0, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int w4a16_marlin_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                      int rows, int cols, w4a16_stream_t stream) {
+  return gemv_common(packed, W4A16_PACK_INTERLEAVED, scale, W4A16_DTYPE_F32, 0, vec, 1, rows, cols,
+                     out, W4A16_DTYPE_F32, nullptr, nullptr, 0, stream);
+}
+
+int w4a16_marlin_g128_cuda(const uint8_t* packed, const float* scale, const void* vec,
+                           float* out, int rows, int cols, w4a16_stream_t stream) {
+  return gemv_common(packed, W4A16_PACK_INTERLEAVED, scale, W4A16_DTYPE_F32, 128, vec, 1, rows,
+                     cols, out, W4A16_DTYPE_F32, nullptr, nullptr, 0, stream);
+}
+
+int w4a16_byte_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                    int rows, int cols, w4a16_stream_t stream) {
+  return ladder(packed, scale, vec, out, rows, cols, stream);
+}
+
+int w4a16_u32_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                   int rows, int cols, w4a16_stream_t stream) {
+  return ladder(packed, scale, vec, out, rows, cols, stream);
+}
+
+int w4a16_u32_v4_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                      int rows, int cols, w4a16_stream_t stream) {
+  return ladder(packed, scale, vec, out, rows, cols, stream);
+}
+
+int w4a16_champ_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                     int rows, int cols, w4a16_stream_t stream) {
+  return ladder(packed, scale, vec, out, rows, cols, stream);
+}
+
+int w4a16_uint4_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                     int rows, int cols, w4a16_stream_t stream) {
+  return ladder(packed, scale, vec, out, rows, cols, stream);
+}
+
+int w4a16_h2f32_cuda(const uint8_t* packed, const float* scale, const void* vec, float* out,
+                     int rows, int cols, w4a16_stream_t stream) {
+  int rc = check_gemv(packed, W4A16_PACK_SIMPLE, scale, W4A16_DTYPE_F32, 0, vec, 1, rows, cols,
+                      out, W4A16_DTYPE_F32);
+  if (rc != W4A16_OK || rows == 0) return rc;
+  return w4a16::launch_h2f32(packed, scale, vec, out, rows, cols,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int w4a16_fp16_cuda(const void* mat, const void* vec, float* out, int rows, int cols,
+                    w4a16_stream_t stream) {
+  if (rows < 0 || cols <= 0 || cols % 8 != 0) {
+    set_error("bad shape rows=%d cols=%d (cols must be a positive multiple of 8)", rows, cols);
+    return W4A16_ERR_SHAPE;
+  }
+  if (rows == 0) return W4A16_OK;
+  if (!mat || !vec || !out) {
+    set_error("NULL pointer");
+    return W4A16_ERR_NULL;
+  }
+  if (!aligned(mat, 16) || !aligned(vec, 16) || !aligned(out, 4)) {
+    set_error("mat and vec must be 16-byte aligned, out 4-byte aligned");
+    return W4A16_ERR_ALIGN;
+  }
+  return w4a16::launch_fp16_gemv(mat, vec, out, rows, cols, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_dtype, int group,
+               const void* x, int batch, int rows, int cols, void* out, int out_dtype,
+               const float* bias, void* workspace, size_t workspace_bytes,
+               w4a16_stream_t stream) {
+  return gemv_common(packed, packing, scale, scale_dtype, group, x, batch, rows, cols, out,
+                     out_dtype, bias, workspace, workspace_bytes, stream);
+}
+
+size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols) {
+  return w4a16::gemv_workspace_bytes(batch, rows, cols);
+}
+
+int w4a16_dequant(const uint8_t* packed, int packing, const void* scale, int scale_dtype,
+                  int group, int rows, int cols, void* out, w4a16_stream_t stream) {
+  int rc = check_gemv(packed, packing, scale, scale_dtype, group, out, 1, rows, cols, out,
+                      W4A16_DTYPE_F16);
+  if (rc != W4A16_OK || rows == 0) return rc;
+  return w4a16::launch_dequant(packed, packing, scale, scale_dtype, group, rows, cols, out,
+                               reinterpret_cast<cudaStream_t>(stream));
+}
+
+int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int group, int packing,
+                        uint8_t* packed, void* scale, int scale_dtype, w4a16_stream_t stream) {
+  if (w_dtype != W4A16_DTYPE_F32 && w_dtype != W4A16_DTYPE_F16) {
+    set_error("unknown weight dtype code %d", w_dtype);
+    return W4A16_ERR_DTYPE;
+  }
+  int rc = check_gemv(packed, packing, scale, scale_dtype, group, packed, 1, rows, cols, packed,
+                      W4A16_DTYPE_F16);
+  if (rc != W4A16_OK || rows == 0) return rc;
+  if (!w) {
+    set_error("NULL weight pointer");
+    return W4A16_ERR_NULL;
+  }
+  if (!aligned(w, w_dtype == W4A16_DTYPE_F32 ? 4 : 2)) {
+    set_error("weight pointer misaligned");
+    return W4A16_ERR_ALIGN;
+  }
+  return w4a16::launch_quantize_pack(w, w_dtype, rows, cols, group, packing, packed, scale,
+                                     scale_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int w4a16_read_device_error(int* code, w4a16_stream_t stream) {
+  if (!code) {
+    set_error("NULL code pointer");
+    return W4A16_ERR_NULL;
+  }
+  return w4a16::read_device_error(code, reinterpret_cast<cudaStream_t>(stream));
+}
+
+const char* w4a16_status_string(int status) {
+  switch (status) {
+    case W4A16_OK: return "ok";
+    case W4A16_ERR_NULL: return "NULL pointer";
+    case W4A16_ERR_SHAPE: return "bad shape";
+    case W4A16_ERR_ALIGN: return "misaligned pointer";
+    case W4A16_ERR_DTYPE: return "unknown dtype, packing or group";
+    case W4A16_ERR_WORKSPACE: return "workspace too small";
+    case W4A16_ERR_CUDA: return "CUDA error";
+    case W4A16_ERR_KERNEL: return "kernel wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* w4a16_last_error_string(void) { return w4a16::last_error(); }
+
+int w4a16_version(void) { return kVersion; }
+
+}  // extern "C"

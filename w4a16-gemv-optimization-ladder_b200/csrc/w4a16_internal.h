@@ -1,0 +1,64 @@
+// Internal (C++) interface between the C-ABI layer (w4a16_capi.cu) and the kernel
+// launchers (w4a16_kernels.cu).  Nothing here crosses the library boundary.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "w4a16_b200.h"
+
+namespace w4a16 {
+
+// One W4A16 product  Y[M][N] = X[M][K] . dequant(W)[N][K]^T  (+ bias), where
+// dequant(W)[r][k] = (q[r][k]) * scale(r, k) and q is the signed int4 code.
+struct GemvProblem {
+  const uint8_t* packed = nullptr;  // [N][K/2] bytes
+  int packing = W4A16_PACK_INTERLEAVED;
+  const void* scale = nullptr;      // [N] (group 0) or [N][K/group]
+  int scale_dtype = W4A16_DTYPE_F32;
+  int group = 0;                    // 0 = one scale per row, 128 = one per 128 columns
+  const void* x = nullptr;          // fp16 [M][K]
+  int M = 1, N = 0, K = 0;
+  void* y = nullptr;                // [M][N], dtype out_dtype
+  int out_dtype = W4A16_DTYPE_F32;
+  const float* bias = nullptr;      // fp32 [N] or null
+  void* workspace = nullptr;        // split-K partials + tile counters (zero-filled once)
+  size_t workspace_bytes = 0;
+  int split_k = 0;                  // 0 = choose, 1 = off, >1 = requested split count
+  cudaStream_t stream = nullptr;
+};
+
+// Validated launch of the W4A16 product.  Chooses the TMA/tensor-core kernel when
+// the shape and alignment allow it, else the generic warp-per-row kernel.
+int launch_gemv(const GemvProblem& p);
+
+// Workspace the split-K path may use for a problem of this size.
+size_t gemv_workspace_bytes(int M, int N, int K);
+
+// fp16 products summed in fp16 per packed word (the lossy variant), simple packing.
+int launch_h2f32(const uint8_t* packed, const float* scale, const void* vec, float* out, int rows,
+                 int cols, cudaStream_t stream);
+
+// Dense fp16 matrix-vector product with fp32 accumulation (bandwidth baseline).
+int launch_fp16_gemv(const void* mat, const void* vec, float* out, int rows, int cols,
+                     cudaStream_t stream);
+
+// Bit-exact dequantisation: out[r][k] = fp16(fp32(q[r][k]) * fp32(scale(r, k))).
+int launch_dequant(const uint8_t* packed, int packing, const void* scale, int scale_dtype,
+                   int group, int rows, int cols, void* out, cudaStream_t stream);
+
+// Symmetric int4 quantisation + packing on the GPU (one launch):
+//   scale = absmax / 7 per row or group, q = clamp(rint(w / scale), -8, 7).
+int launch_quantize_pack(const void* w, int w_dtype, int rows, int cols, int group, int packing,
+                         uint8_t* packed, void* scale, int scale_dtype, cudaStream_t stream);
+
+// Reads (and clears) the device-side error word written by kernels whose bounded
+// waits ran out.  Synchronises `stream`.
+int read_device_error(int* code, cudaStream_t stream);
+
+// Thread-local description of the last failure, for w4a16_last_error_string().
+void set_error(const char* fmt, ...);
+const char* last_error();
+
+}  // namespace w4a16
