@@ -58,7 +58,7 @@ class ClockSampler(threading.Thread):
         self.samples = []
         self.sm_max = None
         self.error = None
-        self._stop = threading.Event()
+        self._halt = threading.Event()
         self._handle = None
         try:
             import pynvml
@@ -78,7 +78,7 @@ class ClockSampler(threading.Thread):
         if self._handle is None:
             return
         nv = self._nvml
-        while not self._stop.is_set():
+        while not self._halt.is_set():
             try:
                 sm = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
                 try:
@@ -92,7 +92,7 @@ class ClockSampler(threading.Thread):
             time.sleep(self.period)
 
     def stop(self):
-        self._stop.set()
+        self._halt.set()
         self.join(timeout=2)
 
     def summary(self):

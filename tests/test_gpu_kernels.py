@@ -42,8 +42,10 @@ def assert_close(y, ref, atol=ATOL, rtol=RTOL, what=""):
     err = np.abs(y - ref)
     bound = atol + rtol * np.abs(ref)
     bad = err > bound
+    idx = np.flatnonzero(bad)[:8]
     assert not bad.any(), (f"{what}: {bad.sum()} of {bad.size} outside tolerance, "
-                           f"max abs err {err.max():.3e}")
+                           f"max abs err {err.max():.3e}; first bad flat indices {idx.tolist()} "
+                           f"got {y.ravel()[idx].tolist()} want {ref.ravel()[idx].tolist()}")
 
 
 def _setup(rows, cols, seed=0):
@@ -202,14 +204,14 @@ FULL = [
 def test_full_size_vs_oracle(rows, cols, group, outliers):
     w, x = _weights(rows, cols, seed=rows + cols + group, outliers=outliers)
     packed, scale = K.quantize_pack(w, group=group)
-    # the GPU quantiser against the reference-identical torch quantiser + packer
-    if group:
-        q_t, s_t = K.quantize_int4_group(w.float(), group=group)
-    else:
-        q_t, s_t = K.quantize_int4_symmetric(w.float())
-    assert torch.equal(packed, K.pack_int4_interleaved(q_t)), "GPU quantize_pack != torch path"
-    assert torch.equal(scale, s_t)
-    del q_t, s_t
+    # the GPU quantiser against the C oracle's (the reference's CPU semantics: true
+    # fp32 division; torch on CUDA divides by the scalar 7 through a reciprocal, so the
+    # reference quantiser run on a GPU tensor can differ from its CPU run in the last
+    # bit of a scale)
+    p_o, s_o = c_oracle.quantize_pack(w.float().cpu().numpy(), group=group)
+    np.testing.assert_array_equal(packed.cpu().numpy(), p_o)
+    np.testing.assert_array_equal(scale.cpu().numpy(), s_o)
+    del p_o, s_o
     y = K.w4a16_gemv_g128(packed, scale, x) if group else K.w4a16_gemv(packed, scale, x)
     ref = c_oracle.gemv(packed.cpu().numpy(), scale.cpu().numpy(), x.cpu().numpy(), group=group)
     assert_close(y.cpu().numpy(), ref, what=f"{rows}x{cols} g{group}")

@@ -60,6 +60,11 @@ constexpr int kTileRows = 16;     // rows per item (the M of one m16n8k16)
 constexpr int kSlabCols = 256;    // columns per 128-byte TMA box row
 constexpr int kSlabBytes = kTileRows * 128;
 constexpr int kMaxBatchPerPass = 16;
+// Split-K workspace layout: [tile counters: kMaxSplitTiles x u32][fp32 partials].
+// The counter region has a fixed size so that calls of different shapes sharing one
+// workspace never see another call's partials where they expect zeroed counters.
+constexpr int kMaxSplitTiles = 4096;
+constexpr size_t kCounterBytes = (size_t)kMaxSplitTiles * 4;
 
 struct TmaParams {
   const void* scale_rows;  // per-row scale [N] (group 0)
@@ -562,8 +567,7 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, int nsplit
   if (nsplit > 1) {
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
     prm.counters = reinterpret_cast<unsigned*>(ws);
-    const size_t cbytes = ((size_t)prm.ntiles * 4 + 255) / 256 * 256;
-    prm.partial = reinterpret_cast<float*>(ws + cbytes);
+    prm.partial = reinterpret_cast<float*>(ws + kCounterBytes);
   }
   int grid = (prm.n_items + kWarps - 1) / kWarps;
   if (prm.n_items >= di.sms) grid = di.sms;
@@ -583,10 +587,6 @@ int launch_generic(const GemvProblem& p, const __half* x, int M, void* y) {
   return check_launch("k_gemv_generic");
 }
 
-size_t counters_bytes(int N) {
-  const size_t ntiles = (size_t)(N + kTileRows - 1) / kTileRows;
-  return (ntiles * 4 + 255) / 256 * 256;
-}
 
 template <int PACK, int GS, typename ST, typename OT>
 int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma,
@@ -607,9 +607,10 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
   const int nstages = (p.K + kStageCols - 1) / kStageCols;
   int nsplit = 1;
   if (p.split_k == 0) {
-    nsplit = choose_split(ntiles, nstages, di.sms * kWarps);
+    nsplit = ntiles <= kMaxSplitTiles ? choose_split(ntiles, nstages, di.sms * kWarps) : 1;
   } else {
     nsplit = p.split_k < nstages ? p.split_k : nstages;
+    if (ntiles > kMaxSplitTiles) nsplit = 1;
   }
   int sps = nstages;
   if (nsplit > 1) {
@@ -617,7 +618,7 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
     nsplit = (nstages + sps - 1) / sps;
   }
   if (nsplit > 1) {
-    const size_t need = counters_bytes(p.N) + (size_t)nsplit * M * p.N * 4;
+    const size_t need = kCounterBytes + (size_t)nsplit * M * p.N * 4;
     if (!p.workspace || p.workspace_bytes < need || !aligned(p.workspace, 256)) {
       if (p.split_k > 1) {
         set_error("split-K %d needs a 256-byte aligned workspace of %zu bytes (got %zu)",
@@ -662,7 +663,7 @@ size_t gemv_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int mc = M < kMaxBatchPerPass ? M : kMaxBatchPerPass;
   const size_t nstages = (size_t)(K + kStageCols - 1) / kStageCols;
-  return counters_bytes(N) + nstages * (size_t)mc * N * 4;
+  return kCounterBytes + nstages * (size_t)mc * N * 4;
 }
 
 int launch_gemv(const GemvProblem& p) {
