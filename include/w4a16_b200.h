@@ -118,6 +118,18 @@ int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_
 /* Bytes of workspace that let w4a16_gemv use split-K for this problem size. */
 size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols);
 
+/* No counterpart in the reference.  The same product as w4a16_gemv (interleaved
+ * packing, one activation vector, fp32 out, no bias) for callers that cannot
+ * allocate device memory — a runtime that fixes its memory plan at start-up, or a
+ * plugin interface that passes only input and output buffers.  Split-K scratch comes
+ * from a 4 MiB array inside the library (one per GPU that loads it, kept until exit),
+ * so nothing is allocated.  Limit: 16384 + 4*rows*ceil(cols/1024) <= 4 MiB, else
+ * W4A16_ERR_WORKSPACE and nothing runs.  The first call on a device looks up the
+ * array's address; make it before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race, so order them on one stream. */
+int w4a16_gemv_noalloc(const uint8_t* packed, const void* scale, int scale_dtype, int group,
+                       const void* x, int rows, int cols, float* out, w4a16_stream_t stream);
+
 /* out[r][k] = fp16( fp32(q[r][k]) * fp32(scale(r, k)) ), fp16 [rows][cols], one
  * round-to-nearest per step: bit-identical to (q.float() * scale_expanded).half()
  * computed from the reference's dequant formula (src/w4a16/kernels.py:94-101). */

@@ -659,6 +659,8 @@ void set_error(const char* fmt, ...) {
 
 const char* last_error() { return t_last_error; }
 
+size_t gemv_counter_bytes() { return kCounterBytes; }
+
 size_t gemv_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int mc = M < kMaxBatchPerPass ? M : kMaxBatchPerPass;

@@ -36,6 +36,10 @@ int launch_gemv(const GemvProblem& p);
 // Workspace the split-K path may use for a problem of this size.
 size_t gemv_workspace_bytes(int M, int N, int K);
 
+// Bytes at the start of a split-K workspace holding the per-tile counters, which
+// must be zero when a kernel starts (the kernels leave them zeroed).
+size_t gemv_counter_bytes();
+
 // fp16 products summed in fp16 per packed word (the lossy variant), simple packing.
 int launch_h2f32(const uint8_t* packed, const float* scale, const void* vec, float* out, int rows,
                  int cols, cudaStream_t stream);

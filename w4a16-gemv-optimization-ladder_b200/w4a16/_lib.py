@@ -36,6 +36,7 @@ SIGNATURES = {
     "w4a16_fp16_cuda": ([_p, _p, _p, _i, _i, _p], _i),
     "w4a16_gemv": ([_p, _i, _p, _i, _i, _p, _i, _i, _i, _p, _i, _p, _p, _sz, _p], _i),
     "w4a16_gemv_workspace_bytes": ([_i, _i, _i], _sz),
+    "w4a16_gemv_noalloc": ([_p, _p, _i, _i, _p, _i, _i, _p, _p], _i),
     "w4a16_dequant": ([_p, _i, _p, _i, _i, _i, _i, _p, _p], _i),
     "w4a16_quantize_pack": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p], _i),
     "w4a16_read_device_error": ([ctypes.POINTER(ctypes.c_int), _p], _i),
