@@ -215,15 +215,20 @@ def run_ours(args, rank, world, dev):
     L = _lib.lib()
     sptr = ctypes.c_void_p(stream.cuda_stream)
 
+    ws = torch.zeros(int(L.w4a16_gemv_workspace_bytes(1, ROWS, COLS)), dtype=torch.uint8, device=dev)
+
     def gemv_fn(packed, scale, out, group):
-        entry = L.w4a16_marlin_g128_cuda if group else L.w4a16_marlin_cuda
-        args_ = (ctypes.c_void_p(packed.data_ptr()), ctypes.c_void_p(scale.data_ptr()),
-                 ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()), packed.shape[0],
-                 packed.shape[1] * 2)
+        # the library's general C entry point (w4a16_gemv), with its workspace, as the
+        # Python op w4a16.w4a16_gemv_g128 calls it
+        args_ = (ctypes.c_void_p(packed.data_ptr()), _lib.PACK_INTERLEAVED,
+                 ctypes.c_void_p(scale.data_ptr()), _lib.DTYPE_F32, group,
+                 ctypes.c_void_p(x.data_ptr()), 1, packed.shape[0], packed.shape[1] * 2,
+                 ctypes.c_void_p(out.data_ptr()), _lib.DTYPE_F32, None,
+                 ctypes.c_void_p(ws.data_ptr()), ws.numel())
 
         def f():
             s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-            st = entry(*args_, s)
+            st = L.w4a16_gemv(*args_, s)
             if st != 0:
                 raise RuntimeError(L.w4a16_last_error_string().decode())
         return f
@@ -417,7 +422,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=4000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -465,7 +470,7 @@ def main():
                    "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
                    "value_definition": "device time per 262144x2048 GEMV-equivalent (step time / GEMVs per step)",
                    "l2": "inputs larger than L2: 2 rotating copies of 285 MB packed weights+scales",
-                   "timing": "CUDA events around CUDA-graph replays of K launches"},
+                   "timing": "CUDA events around CUDA-graph replays of K launches of the C entry w4a16_gemv"},
         "roofline": res["roofline"],
         "cpu_baseline": res.get("cpu_baseline"),
         "e2e": res["e2e"],

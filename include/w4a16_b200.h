@@ -107,15 +107,19 @@ int w4a16_fp16_cuda(const void* mat, const void* vec, float* out, int rows, int 
  * applies at src/w4a16/kernels.py:122-124), and split-K for short-row layers.
  *   group      0 (one scale per row) or 128 (one scale per 128 columns)
  *   workspace  NULL, or a zero-filled device buffer of workspace_bytes; when at
- *              least w4a16_gemv_workspace_bytes(batch, rows, cols) it enables the
- *              split-K path for layers with few rows.  The kernels leave it zeroed.
- *              Calls that share a workspace must be ordered on one stream. */
+ *              least w4a16_gemv_workspace_bytes(batch, rows, cols) it lets every
+ *              warp take an equal share of the work (tiles shared by two warps are
+ *              reduced through it); without it each warp owns whole 16-row tiles.
+ *              The kernels leave it zeroed.  Calls that share a workspace must be
+ *              ordered on one stream. */
 int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_dtype, int group,
                const void* x, int batch, int rows, int cols, void* out, int out_dtype,
                const float* bias, void* workspace, size_t workspace_bytes,
                w4a16_stream_t stream);
 
-/* Bytes of workspace that let w4a16_gemv use split-K for this problem size. */
+/* Bytes of workspace that let w4a16_gemv balance its work across warps (stream-K)
+ * for this batch size; independent of rows and cols (about 0.5 MiB per activation
+ * row, at most 16 of them per pass). */
 size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols);
 
 /* No counterpart in the reference.  The same product as w4a16_gemv (interleaved
@@ -123,8 +127,9 @@ size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols);
  * allocate device memory — a runtime that fixes its memory plan at start-up, or a
  * plugin interface that passes only input and output buffers.  Split-K scratch comes
  * from a 4 MiB array inside the library (one per GPU that loads it, kept until exit),
- * so nothing is allocated.  Limit: 16384 + 4*rows*ceil(cols/1024) <= 4 MiB, else
- * W4A16_ERR_WORKSPACE and nothing runs.  The first call on a device looks up the
+ * so nothing is allocated.  The scratch a call needs (w4a16_gemv_workspace_bytes(1,
+ * rows, cols), about 0.5 MiB) does not grow with the matrix; a call needing more than
+ * 4 MiB would get W4A16_ERR_WORKSPACE with nothing run.  The first call on a device looks up the
  * array's address; make it before any stream capture.  All calls share the array:
  * calls that overlap on the GPU race, so order them on one stream. */
 int w4a16_gemv_noalloc(const uint8_t* packed, const void* scale, int scale_dtype, int group,

@@ -267,7 +267,8 @@ def test_fp16_scales_and_fp16_bias_epilogue(group):
 # ------------------------------------------------------------- edge shapes
 
 EDGE = [(1, 256, 0), (17, 256, 0), (33, 512, 128), (5, 8, 0), (3, 24, 0), (7, 136, 0),
-        (4, 128, 128), (19, 384, 128), (100, 768, 0), (1000, 11008, 0)]
+        (4, 128, 128), (19, 384, 128), (100, 768, 0), (1000, 11008, 0), (300, 14336, 128),
+        (70, 16384, 0)]
 
 
 @pytest.mark.parametrize("rows,cols,group", EDGE, ids=[f"{r}x{c}-g{g}" for r, c, g in EDGE])

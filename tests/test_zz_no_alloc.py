@@ -55,15 +55,19 @@ def test_noalloc_matches_workspace_entry_two_calls(rows, cols, group, sdt):
         assert (err <= ATOL + RTOL * np.abs(ref)).all(), f"max abs err {err.max():.3e}"
 
 
-def test_noalloc_rejects_oversize_without_running():
-    packed = torch.zeros(16, 4096, dtype=torch.uint8, device=DEV)
-    scale = torch.ones(16, device=DEV)
-    x = torch.zeros(8192, dtype=torch.float16, device=DEV)
-    out = torch.full((16,), 7.0, device=DEV)
-    # 600000 rows x 8192 columns would need ~19 MB of scratch: rejected on the host
-    st = _lib.lib().w4a16_gemv_noalloc(_p(packed), _p(scale), 0, 0, _p(x), 600000, 8192, _p(out),
-                                       None)
-    assert st == -5  # W4A16_ERR_WORKSPACE
-    assert b"static array" in _lib.lib().w4a16_last_error_string()
-    torch.cuda.synchronize()
-    assert (out == 7.0).all()
+def test_noalloc_scratch_does_not_grow_with_the_matrix():
+    # the scratch need is set by the warp count, not by rows x cols: the largest
+    # shape of the benchmark runs through the static array as well
+    L = _lib.lib()
+    assert L.w4a16_gemv_workspace_bytes(1, 262144, 2048) == L.w4a16_gemv_workspace_bytes(1, 2048, 8192)
+    assert L.w4a16_gemv_workspace_bytes(1, 262144, 2048) <= 4 << 20
+    g = torch.Generator(device=DEV).manual_seed(5)
+    w = (torch.randn(262144, 2048, device=DEV, generator=g) * 0.02).half()
+    x = torch.randn(2048, device=DEV, generator=g).half()
+    packed, scale = K.quantize_pack(w, group=128)
+    del w
+    ref = K.gemv(packed, scale, x, group=128).cpu().numpy().astype(np.float64)
+    for _ in range(2):
+        y = _noalloc(packed, scale, x, 128).cpu().numpy().astype(np.float64)
+        err = np.abs(y - ref)
+        assert (err <= ATOL + RTOL * np.abs(ref)).all(), f"max abs err {err.max():.3e}"

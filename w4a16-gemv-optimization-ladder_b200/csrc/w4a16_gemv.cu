@@ -2,16 +2,20 @@
 //
 // Main path (k_gemv_tma): every warp owns a private ring of shared-memory stages
 // that TMA (cp.async.bulk.tensor, 128-byte swizzle) fills with 16-row x 1024-column
-// tiles of packed int4 weights (and, for group-128, the matching scale tile).  The
-// warp decodes each packed word to f16x2 codes in registers (decode_word: shift +
-// 4 lop3 + 4 f16x2 ops, exact) and feeds them as the A operand of
-// mma.sync.m16n8k16 with the activation as the B operand, so products are exact and
-// accumulation is fp32 in the tensor core.  Columns of B carry up to 8 (16 with two
-// MMAs) activation rows: batch 1..16 costs the same weight traffic as batch 1.
-// Group-128 partial sums are scaled in fp32 once per group; per-row sums once per
-// row.  Items (16 rows x a K range) are spread warp-major over a persistent grid of
-// one CTA per SM; layers with few rows split K across warps and the last warp to
-// finish a tile reduces the partials in a fixed order (deterministic).
+// windows of packed int4 weights (one 3-D box per window) and, for group-128, the
+// matching scale tile.  The warp decodes each packed word to f16x2 codes in
+// registers (decode_word: shift + 4 lop3 + 4 f16x2 ops, exact) and feeds them as the
+// A operand of mma.sync.m16n8k16 with the activation as the B operand, so products
+// are exact and accumulation is fp32 in the tensor core.  Columns of B carry up to
+// 8 (16 with two MMAs) activation rows: batch 1..16 costs the same weight traffic
+// as batch 1.  Group-128 partial sums are scaled in fp32 once per group; per-row
+// sums once per row.
+//
+// Scheduling is stream-K over (tile, 256-column slab) units: a persistent grid of
+// one CTA per SM gives every warp an equal contiguous range of units, so all warps
+// finish together whatever the shape.  A tile split between neighbouring warps is
+// finished by the last of them, which adds the published partial sums in warp
+// order (deterministic).  Without a workspace each warp owns whole tiles instead.
 //
 // Reference counterparts: k_marlin (kernels/w4a16_kernels.cu:100-114) and
 // k_marlin_g128 (:121-138) compute the same sums with one warp per row, 4-byte
@@ -33,14 +37,18 @@
 #include "w4a16_internal.h"
 
 #ifndef W4A16_TMA_WARPS
-#define W4A16_TMA_WARPS 8
+#define W4A16_TMA_WARPS 12
 #endif
 #ifndef W4A16_TMA_STAGES
-#define W4A16_TMA_STAGES 3
+#define W4A16_TMA_STAGES 2
 #endif
 #ifndef W4A16_TMA_SLABS
 #define W4A16_TMA_SLABS 4
 #endif
+#ifndef W4A16_TMA_RT
+#define W4A16_TMA_RT 1
+#endif
+
 
 namespace w4a16 {
 
@@ -56,34 +64,54 @@ constexpr uint64_t kDrainWaitLimitNs = 100000000ull;   // 0.1 s per outstanding 
 
 __device__ __forceinline__ void record_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
-constexpr int kTileRows = 16;     // rows per item (the M of one m16n8k16)
-constexpr int kSlabCols = 256;    // columns per 128-byte TMA box row
-constexpr int kSlabBytes = kTileRows * 128;
+constexpr int kMmaRows = 16;      // rows of one m16n8k16 A fragment
+constexpr int kSlabCols = 256;    // columns per 128-byte slab of a packed row
 constexpr int kMaxBatchPerPass = 16;
-// Split-K workspace layout: [tile counters: kMaxSplitTiles x u32][fp32 partials].
-// The counter region has a fixed size so that calls of different shapes sharing one
-// workspace never see another call's partials where they expect zeroed counters.
-constexpr int kMaxSplitTiles = 4096;
-constexpr size_t kCounterBytes = (size_t)kMaxSplitTiles * 4;
+// Stream-K workspace layout: [per-warp counters: kMaxWarps x u32][fp32 partials:
+// kMaxWarps x 2 slots x batch x tile rows].  Both regions have a size fixed by
+// kMaxWarps, not by the problem, so calls of any shape can share one workspace.
+constexpr int kMaxWarps = 4096;
+constexpr size_t kCounterBytes = (size_t)kMaxWarps * 4;
 
 struct TmaParams {
   const void* scale_rows;  // per-row scale [N] (group 0)
   const __half* x;         // [M][K]
   void* y;                 // [M][N]
   const float* bias;       // [N] or null
-  float* partial;          // [nsplit][M][N] when nsplit > 1
-  unsigned* counters;      // [ntiles] when nsplit > 1
+  float* partial;          // [nwarps][2][M][tile rows] (stream-K mode)
+  unsigned* counters;      // [nwarps] (stream-K mode)
+  long long units;         // ntiles * nwin
   int M, N, K;
-  int ntiles, nsplit, stages_per_split, nstages, n_items;
+  int ntiles, kslabs, nwin;
+  int nwarps;              // warps that receive work
+  int aligned;             // 1: each warp owns whole tiles (no workspace needed)
 };
 
-template <int SLABS, int GS, typename ST>
+// Shared-memory stage of one warp: a window of SLABS 256-column slabs of RT*16 rows,
+// one 3-D TMA box laid out [row][slab][128 B] with the 128-byte swizzle (1024-byte
+// aligned), so every row of the box is one 512-byte run of global memory; and, for
+// group-128, the window's scale tile [row][2*SLABS].
+template <int SLABS, int RT, int GS, typename ST>
 struct StageLayout {
-  static constexpr int kWBytes = SLABS * kSlabBytes;
-  static constexpr int kGroups = SLABS * 2;  // 128-column groups per stage
-  static constexpr int kSBytes = GS ? kTileRows * kGroups * (int)sizeof(ST) : 0;
-  static constexpr int kBytes = (kWBytes + kSBytes + 1023) / 1024 * 1024;
+  static_assert(SLABS == 4, "the swizzled [row][slab] layout is bank-conflict free for 4 slabs");
+  static constexpr int kRows = kMmaRows * RT;
+  static constexpr int kWBytes = kRows * SLABS * 128;
+  static constexpr int kWStride = (kWBytes + 1023) / 1024 * 1024;
+  static constexpr int kGroups = SLABS * 2;  // 128-column groups per window
+  static constexpr int kSBytes = GS ? kRows * kGroups * (int)sizeof(ST) : 0;
+  static constexpr int kSStride = (kSBytes + 127) / 128 * 128;
+  static constexpr bool kScaleBoxOk = !GS || (kGroups * sizeof(ST)) % 16 == 0;
 };
+
+// Byte offset of logical 16-byte chunk c of (row r, slab sl) inside a stage.  The
+// 128-byte swizzle puts chunk c of 128-byte smem line L at c ^ (L & 7), L = 4r + sl:
+// rows g and g+8 of one MMA get the same XOR, and the two rows a quarter-warp reads
+// (g even and odd) get XORs that differ in bit 2, so its 8 lanes hit 8 bank groups.
+template <int SLABS>
+__device__ __forceinline__ uint32_t w_offset(int r, int sl, int c) {
+  const int line = r * SLABS + sl;
+  return (uint32_t)(line * 128 + ((c ^ (line & 7)) << 4));
+}
 
 template <int NB>
 struct BatchCfg {
@@ -100,27 +128,148 @@ __device__ __forceinline__ uint4 load_x(const __half* x, int K, int M, int g, in
   return make_uint4(0u, 0u, 0u, 0u);
 }
 
-template <int PACK, int GS, typename ST, int NB, typename OT, int WARPS, int STAGES, int SLABS>
+// One window of one warp: nslab (== SLABS when FULL) slabs of RT*16 rows.
+// Shared-memory copy of a single activation vector, ordered so that the B fragment
+// of (128-column group G, chunk j, thread t) is 16 bytes at ((G*4 + j)*4 + t)*16: the
+// four threads of a group read 64 contiguous bytes, one conflict-free wavefront.
+__device__ __forceinline__ uint32_t xs_offset(int col) {
+  const int grp = col >> 7, off = col & 127;
+  return (uint32_t)(((grp * 4 + ((off & 31) >> 3)) * 4 + (off >> 5)) * 16);
+}
+
+template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS>
+__device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, uint32_t xs,
+                                               int nslab, int kcol0, const TmaParams& p, int g,
+                                               int t, float (&acc)[RT][2][BatchCfg<NB>::kHalves][4],
+                                               float (&tot)[RT][BatchCfg<NB>::kHalves][4]) {
+  constexpr int NH = BatchCfg<NB>::kHalves;
+  constexpr int kGroups = SLABS * 2;
+#pragma unroll
+  for (int sl = 0; sl < SLABS; ++sl) {
+    if (FULL || sl < nslab) {
+      const int kcol = kcol0 + sl * kSlabCols;
+      uint4 wa[RT][2], wb[RT][2];
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int gh = 0; gh < 2; ++gh) {
+          const int c = gh * 4 + t;
+          wa[rt][gh] = lds128(wbase + w_offset<SLABS>(rt * 16 + g, sl, c));
+          wb[rt][gh] = lds128(wbase + w_offset<SLABS>(rt * 16 + g + 8, sl, c));
+        }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int gh = 0; gh < 2; ++gh) {
+          const int col = kcol + gh * 128 + 32 * t + 8 * j;
+          uint4 xv[NH];
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            xv[h] = XS ? lds128(xs + xs_offset(col)) : load_x<NB>(p.x, p.K, p.M, g, h, col);
+            if (PACK == W4A16_PACK_SIMPLE) xv[h] = simple_order(xv[h]);
+          }
+#pragma unroll
+          for (int rt = 0; rt < RT; ++rt) {
+            const uint4& va = wa[rt][gh];
+            const uint4& vb = wb[rt][gh];
+            const uint32_t word_a = j == 0 ? va.x : j == 1 ? va.y : j == 2 ? va.z : va.w;
+            const uint32_t word_b = j == 0 ? vb.x : j == 1 ? vb.y : j == 2 ? vb.z : vb.w;
+            uint32_t A[4], B[4];
+            decode_word(word_a, A);
+            decode_word(word_b, B);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+              if (GS && j == 0)
+                mma_16816_zc(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
+              else
+                mma_16816(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
+              mma_16816(acc[rt][gh][h], A[2], B[2], A[3], B[3], xv[h].z, xv[h].w);
+            }
+          }
+        }
+      }
+      if (GS) {
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+          for (int gh = 0; gh < 2; ++gh) {
+            const int grp = sl * 2 + gh;
+            const int ra = rt * 16 + g;
+            float s0, s1;
+            if (sizeof(ST) == 4) {
+              s0 = lds_f32(sbase + (ra * kGroups + grp) * 4);
+              s1 = lds_f32(sbase + ((ra + 8) * kGroups + grp) * 4);
+            } else {
+              s0 = __half2float(__ushort_as_half(lds_u16(sbase + (ra * kGroups + grp) * 2)));
+              s1 = __half2float(__ushort_as_half(lds_u16(sbase + ((ra + 8) * kGroups + grp) * 2)));
+            }
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+              tot[rt][h][0] = fmaf(s0, acc[rt][gh][h][0], tot[rt][h][0]);
+              tot[rt][h][1] = fmaf(s0, acc[rt][gh][h][1], tot[rt][h][1]);
+              tot[rt][h][2] = fmaf(s1, acc[rt][gh][h][2], tot[rt][h][2]);
+              tot[rt][h][3] = fmaf(s1, acc[rt][gh][h][3], tot[rt][h][3]);
+            }
+          }
+      }
+    }
+  }
+}
+
+// Warp owning unit u of a range split [floor(w*U/T), floor((w+1)*U/T)).
+__device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
+  return (int)(((u + 1) * (long long)T - 1) / U);
+}
+
+template <int PACK, int GS, typename ST, int NB, typename OT, int WARPS, int STAGES, int SLABS, int RT,
+          bool XS>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     k_gemv_tma(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const TmaParams p) {
-  using L = StageLayout<SLABS, GS, ST>;
+  using L = StageLayout<SLABS, RT, GS, ST>;
   constexpr int NH = BatchCfg<NB>::kHalves;
-  static_assert(!GS || (L::kGroups * sizeof(ST)) % 16 == 0, "scale box row must be 16-byte multiple");
+  constexpr int kRows = L::kRows;
+  static_assert(L::kScaleBoxOk, "scale box row must be a 16-byte multiple");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int g = lane >> 2;  // MMA group id: rows g and g+8 of the tile
+  const int g = lane >> 2;  // MMA group id: rows g and g+8 of each 16-row block
   const int t = lane & 3;   // thread in group: 32-column chunk t of each 128-column group
 
-  const int gw = warp * gridDim.x + blockIdx.x;  // warp-major: items spread over all SMs
-  if (gw >= p.n_items) return;
-  const int total_warps = gridDim.x * WARPS;
+  // XS: the CTA first copies the activation vector into shared memory (fragment
+  // order, see xs_offset); every B fragment is then one shared-memory load.
+  const uint32_t xs = base + (uint32_t)(WARPS * STAGES * (L::kWStride + L::kSStride + 8));
+  if (XS) {
+    uint8_t* xsp = smem_raw + (xs - smem_addr(smem_raw));
+    for (int c = threadIdx.x; c < (p.K >> 3); c += blockDim.x)
+      *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = ldg128(p.x + c * 8);
+    __syncthreads();
+  }
 
-  const uint32_t ring = base + (uint32_t)(warp * STAGES * L::kBytes);
-  const uint32_t bar0 = base + (uint32_t)(WARPS * STAGES * L::kBytes + warp * STAGES * 8);
+  const int gw = warp * gridDim.x + blockIdx.x;  // warp-major: ranges spread over all SMs
+  if (gw >= p.nwarps) return;
+  const int ks = p.kslabs;
+  const int nwin = p.nwin;
+  const long long U = p.units;
+  const int T = p.nwarps;
+  long long u0, u1;
+  if (p.aligned) {
+    u0 = (long long)gw * p.ntiles / T * nwin;
+    u1 = (long long)(gw + 1) * p.ntiles / T * nwin;
+  } else {
+    u0 = (long long)gw * U / T;
+    u1 = (long long)(gw + 1) * U / T;
+  }
+  if (u0 >= u1) return;
+  const int first_tile = (int)(u0 / nwin);
+  const int first_win = (int)(u0 - (long long)first_tile * nwin);
+  const int count = (int)(u1 - u0);
+
+  const uint32_t wring = base + (uint32_t)(warp * STAGES * L::kWStride);
+  const uint32_t sring = base + (uint32_t)(WARPS * STAGES * L::kWStride + warp * STAGES * L::kSStride);
+  const uint32_t bar0 = base + (uint32_t)(WARPS * STAGES * (L::kWStride + L::kSStride) + warp * STAGES * 8);
 
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(bar0 + 8 * s, 1);
@@ -130,211 +279,172 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   __syncwarp();
   const uint64_t policy = l2_policy_evict_first();
-  const int kslabs = p.K / kSlabCols;
 
-  // Producer cursor (kept identical in every lane; lane 0 issues).
-  int p_item = gw;
-  int p_stage = (p_item % p.nsplit) * p.stages_per_split;
-  int p_end = min(p_stage + p.stages_per_split, p.nstages);
-  uint32_t issued = 0;
-
+  // Producer position (identical in every lane; lane 0 issues the copies).
+  int p_tile = first_tile, p_win = first_win;
+  int issued = 0;
   auto issue_one = [&]() {
-    if (p_item >= p.n_items) return;
-    const uint32_t slot = issued % STAGES;
+    if (issued >= count) return;
+    const uint32_t slot = (uint32_t)issued % STAGES;
     if (lane == 0) {
-      const int tile = p_item / p.nsplit;
-      const int nslab = min(SLABS, kslabs - p_stage * SLABS);
-      const uint32_t dst = ring + slot * L::kBytes;
+      const int row0 = p_tile * kRows;
+      const int s0 = p_win * SLABS;
       const uint32_t bar = bar0 + 8 * slot;
-      mbar_arrive_expect_tx(bar, (uint32_t)(nslab * kSlabBytes + L::kSBytes));
-      for (int sl = 0; sl < nslab; ++sl)
-        tma_load_2d(dst + sl * kSlabBytes, &wmap, (p_stage * SLABS + sl) * 128, tile * kTileRows,
-                    bar, policy);
-      if (GS) tma_load_2d(dst + L::kWBytes, &smap, p_stage * L::kGroups, tile * kTileRows, bar, policy);
+      const uint32_t dst = wring + slot * L::kWStride;
+      // the full box is credited, including slabs past K that TMA fills with zeros
+      mbar_arrive_expect_tx(bar, (uint32_t)(L::kWBytes + L::kSBytes));
+      tma_load_3d(dst, &wmap, 0, s0, row0, bar, policy);
+      if (GS) tma_load_2d(sring + slot * L::kSStride, &smap, p_win * L::kGroups, row0, bar, policy);
     }
     ++issued;
-    if (++p_stage == p_end) {
-      p_item += total_warps;
-      p_stage = (p_item % p.nsplit) * p.stages_per_split;
-      p_end = min(p_stage + p.stages_per_split, p.nstages);
+    if (++p_win == nwin) {
+      p_win = 0;
+      ++p_tile;
     }
   };
 
 #pragma unroll 1
   for (int s = 0; s < STAGES; ++s) issue_one();
 
-  uint32_t consumed = 0;
-#pragma unroll 1
-  for (int item = gw; item < p.n_items; item += total_warps) {
-    const int tile = item / p.nsplit;
-    const int split = item % p.nsplit;
-    const int st_begin = split * p.stages_per_split;
-    const int st_end = min(st_begin + p.stages_per_split, p.nstages);
-    const int r0 = tile * kTileRows + g;
-    const int r1 = r0 + 8;
-
-    // Per-row scales are needed only in the epilogue: fetch them now.
-    float srow0 = 1.f, srow1 = 1.f;
-    if (!GS) {
-      const ST* sr = static_cast<const ST*>(p.scale_rows);
-      if (r0 < p.N) srow0 = to_f32<ST>(__ldg(sr + r0));
-      if (r1 < p.N) srow1 = to_f32<ST>(__ldg(sr + r1));
-    }
-
-    float tot[NH][4];
-    float acc[2][NH][4];
-#pragma unroll
-    for (int h = 0; h < NH; ++h)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        tot[h][i] = 0.f;
-        acc[0][h][i] = 0.f;
-        acc[1][h][i] = 0.f;
-      }
+  float tot[RT][NH][4];
+  float acc[RT][2][NH][4];
+  float srow[RT][2];
+  int tile = first_tile, win = first_win, tile_w0 = first_win;
 
 #pragma unroll 1
-    for (int stage = st_begin; stage < st_end; ++stage) {
-      const uint32_t slot = consumed % STAGES;
-      const uint32_t parity = (consumed / STAGES) & 1u;
-      if (!mbar_wait_bounded(bar0 + 8 * slot, parity, kStageWaitLimitNs)) {
-        record_device_error(kDevErrStageTimeout);
-        for (uint32_t s = consumed + 1; s < issued; ++s)
-          mbar_wait_bounded(bar0 + 8 * (s % STAGES), (s / STAGES) & 1u, kDrainWaitLimitNs);
-        return;
-      }
-      const uint32_t sbase = ring + slot * L::kBytes;
-      const int nslab = min(SLABS, kslabs - stage * SLABS);
-
+  for (int consumed = 0; consumed < count; ++consumed) {
+    if (win == 0 || consumed == 0) {  // a tile starts in this warp's range
+      tile_w0 = win;
 #pragma unroll
-      for (int sl = 0; sl < SLABS; ++sl) {
-        if (sl < nslab) {
-          const uint32_t slab = sbase + sl * kSlabBytes;
-          const int kcol = (stage * SLABS + sl) * kSlabCols;
-          // 128-byte swizzle: 16-byte chunk c of smem row r sits at chunk c ^ (r & 7).
-          uint4 wa[2], wb[2];
-#pragma unroll
-          for (int gh = 0; gh < 2; ++gh) {
-            const uint32_t c = (uint32_t)((gh * 4 + t) ^ g);
-            wa[gh] = lds128(slab + g * 128 + c * 16);
-            wb[gh] = lds128(slab + (g + 8) * 128 + c * 16);
-          }
-          if (GS) {
-#pragma unroll
-            for (int gh = 0; gh < 2; ++gh)
-#pragma unroll
-              for (int h = 0; h < NH; ++h)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[gh][h][i] = 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int gh = 0; gh < 2; ++gh) {
-              const uint32_t word_a = j == 0 ? wa[gh].x : j == 1 ? wa[gh].y : j == 2 ? wa[gh].z : wa[gh].w;
-              const uint32_t word_b = j == 0 ? wb[gh].x : j == 1 ? wb[gh].y : j == 2 ? wb[gh].z : wb[gh].w;
-              uint32_t A[4], B[4];
-              decode_word(word_a, A);
-              decode_word(word_b, B);
-              const int col = kcol + gh * 128 + 32 * t + 8 * j;
-#pragma unroll
-              for (int h = 0; h < NH; ++h) {
-                uint4 xv = load_x<NB>(p.x, p.K, p.M, g, h, col);
-                if (PACK == W4A16_PACK_SIMPLE) xv = simple_order(xv);
-                mma_16816(acc[gh][h], A[0], B[0], A[1], B[1], xv.x, xv.y);
-                mma_16816(acc[gh][h], A[2], B[2], A[3], B[3], xv.z, xv.w);
-              }
-            }
-          }
-          if (GS) {
-            const uint32_t sb = sbase + L::kWBytes;
-#pragma unroll
-            for (int gh = 0; gh < 2; ++gh) {
-              const int grp = sl * 2 + gh;
-              float s0, s1;
-              if (sizeof(ST) == 4) {
-                s0 = lds_f32(sb + (g * L::kGroups + grp) * 4);
-                s1 = lds_f32(sb + ((g + 8) * L::kGroups + grp) * 4);
-              } else {
-                s0 = __half2float(__ushort_as_half(lds_u16(sb + (g * L::kGroups + grp) * 2)));
-                s1 = __half2float(__ushort_as_half(lds_u16(sb + ((g + 8) * L::kGroups + grp) * 2)));
-              }
-#pragma unroll
-              for (int h = 0; h < NH; ++h) {
-                tot[h][0] = fmaf(s0, acc[gh][h][0], tot[h][0]);
-                tot[h][1] = fmaf(s0, acc[gh][h][1], tot[h][1]);
-                tot[h][2] = fmaf(s1, acc[gh][h][2], tot[h][2]);
-                tot[h][3] = fmaf(s1, acc[gh][h][3], tot[h][3]);
-              }
-            }
-          }
-        }
-      }
-      __syncwarp();  // every lane has read the slot before it is refilled
-      ++consumed;
-      issue_one();
-    }
-
-    if (!GS) {
-#pragma unroll
-      for (int h = 0; h < NH; ++h) {
-        tot[h][0] = (acc[0][h][0] + acc[1][h][0]) * srow0;
-        tot[h][1] = (acc[0][h][1] + acc[1][h][1]) * srow0;
-        tot[h][2] = (acc[0][h][2] + acc[1][h][2]) * srow1;
-        tot[h][3] = (acc[0][h][3] + acc[1][h][3]) * srow1;
-      }
-    }
-
-    // Fragment (h, i): row r0 (i < 2) or r1, batch column n = h*8 + 2t + (i & 1).
-    if (p.nsplit == 1) {
-#pragma unroll
-      for (int h = 0; h < NH; ++h)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = i < 2 ? r0 : r1;
-          const int n = h * 8 + 2 * t + (i & 1);
-          const bool ok = NB == 1 ? (t == 0 && (i & 1) == 0) : (n < p.M);
-          if (ok && r < p.N) {
-            float v = tot[h][i];
-            if (p.bias) v += __ldg(p.bias + r);
-            static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
-          }
-        }
-    } else {
-#pragma unroll
-      for (int h = 0; h < NH; ++h)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = i < 2 ? r0 : r1;
-          const int n = h * 8 + 2 * t + (i & 1);
-          const bool ok = NB == 1 ? (t == 0 && (i & 1) == 0) : (n < p.M);
-          if (ok && r < p.N) p.partial[((size_t)split * p.M + n) * p.N + r] = tot[h][i];
-        }
-      __threadfence();
-      __syncwarp();
-      unsigned prev = 0;
-      if (lane == 0) prev = atomicAdd(p.counters + tile, 1u);
-      prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (prev == (unsigned)(p.nsplit - 1)) {
-        __threadfence();
+      for (int rt = 0; rt < RT; ++rt) {
 #pragma unroll
         for (int h = 0; h < NH; ++h)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int r = i < 2 ? r0 : r1;
+            tot[rt][h][i] = 0.f;
+            acc[rt][0][h][i] = 0.f;
+            acc[rt][1][h][i] = 0.f;
+          }
+        const int r0 = tile * kRows + rt * 16 + g;
+        srow[rt][0] = srow[rt][1] = 1.f;
+        if (!GS) {  // per-row scales are used in the epilogue: fetch them now
+          const ST* sr = static_cast<const ST*>(p.scale_rows);
+          if (r0 < p.N) srow[rt][0] = to_f32<ST>(__ldg(sr + r0));
+          if (r0 + 8 < p.N) srow[rt][1] = to_f32<ST>(__ldg(sr + r0 + 8));
+        }
+      }
+    }
+
+    const uint32_t slot = (uint32_t)consumed % STAGES;
+    const uint32_t parity = ((uint32_t)consumed / STAGES) & 1u;
+    if (!mbar_wait_bounded(bar0 + 8 * slot, parity, kStageWaitLimitNs)) {
+      record_device_error(kDevErrStageTimeout);
+      for (int s = consumed + 1; s < issued; ++s)
+        mbar_wait_bounded(bar0 + 8 * (s % STAGES), (s / STAGES) & 1u, kDrainWaitLimitNs);
+      return;
+    }
+    const uint32_t wbase = wring + slot * L::kWStride;
+    const uint32_t sbase = sring + slot * L::kSStride;
+    const int s0 = win * SLABS;
+    const int nslab = min(SLABS, ks - s0);
+    if (nslab == SLABS)
+      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS>(wbase, sbase, xs, nslab, s0 * kSlabCols,
+                                                            p, g, t, acc, tot);
+    else
+      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS>(wbase, sbase, xs, nslab, s0 * kSlabCols,
+                                                             p, g, t, acc, tot);
+    __syncwarp();  // every lane has read the slot before it is refilled
+    issue_one();
+
+    const int cur_tile = tile;
+    const bool tile_done = win == nwin - 1;
+    if (++win == nwin) {
+      win = 0;
+      ++tile;
+    }
+    if (!tile_done && consumed + 1 < count) continue;  // the tile goes on in this warp
+
+    // ---- tile epilogue
+    if (!GS) {
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          tot[rt][h][0] = (acc[rt][0][h][0] + acc[rt][1][h][0]) * srow[rt][0];
+          tot[rt][h][1] = (acc[rt][0][h][1] + acc[rt][1][h][1]) * srow[rt][0];
+          tot[rt][h][2] = (acc[rt][0][h][2] + acc[rt][1][h][2]) * srow[rt][1];
+          tot[rt][h][3] = (acc[rt][0][h][3] + acc[rt][1][h][3]) * srow[rt][1];
+        }
+    }
+    // Fragment (rt, h, i): row cur_tile*kRows + rt*16 + g (+8 for i >= 2), batch
+    // column n = h*8 + 2t + (i & 1).
+    if (tile_w0 == 0 && tile_done) {  // the whole tile was summed here
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = cur_tile * kRows + rt * 16 + g + (i < 2 ? 0 : 8);
             const int n = h * 8 + 2 * t + (i & 1);
             const bool ok = NB == 1 ? (t == 0 && (i & 1) == 0) : (n < p.M);
             if (ok && r < p.N) {
-              float v = 0.f;
-              for (int s = 0; s < p.nsplit; ++s)
-                v += __ldcg(p.partial + ((size_t)s * p.M + n) * p.N + r);
+              float v = tot[rt][h][i];
               if (p.bias) v += __ldg(p.bias + r);
               static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
             }
           }
-        __syncwarp();
-        if (lane == 0) p.counters[tile] = 0u;  // leave the workspace zeroed
-      }
+      continue;
     }
+    // Part of a tile shared with neighbouring warps: publish the partial sums; the
+    // last contributor adds all of them in warp order and writes the tile.
+    const int slot_out = cur_tile == first_tile ? 0 : 1;
+    float* mine = p.partial + ((size_t)gw * 2 + slot_out) * p.M * kRows;
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < NH; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rl = rt * 16 + g + (i < 2 ? 0 : 8);
+          const int n = h * 8 + 2 * t + (i & 1);
+          const bool ok = NB == 1 ? (t == 0 && (i & 1) == 0) : (n < p.M);
+          if (ok) mine[(size_t)n * kRows + rl] = tot[rt][h][i];
+        }
+    const long long tu0 = (long long)cur_tile * nwin;
+    const int w_first = warp_of_unit(tu0, U, T);
+    const int w_last = warp_of_unit(tu0 + nwin - 1, U, T);
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(p.counters + w_first, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)(w_last - w_first)) continue;
+    __threadfence();
+    // Every contributor after the first starts inside this tile, so the tile is its
+    // first (slot 0); the first contributor used slot 1 unless it also started here.
+    const int slot_first = ((long long)w_first * U / T) / nwin == cur_tile ? 0 : 1;
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < NH; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rl = rt * 16 + g + (i < 2 ? 0 : 8);
+          const int r = cur_tile * kRows + rl;
+          const int n = h * 8 + 2 * t + (i & 1);
+          const bool ok = NB == 1 ? (t == 0 && (i & 1) == 0) : (n < p.M);
+          if (ok && r < p.N) {
+            const size_t off = (size_t)n * kRows + rl;
+            const size_t wstride = (size_t)2 * p.M * kRows;
+            float v = __ldcg(p.partial + ((size_t)w_first * 2 + slot_first) * p.M * kRows + off);
+            for (int w = w_first + 1; w <= w_last; ++w) v += __ldcg(p.partial + (size_t)w * wstride + off);
+            if (p.bias) v += __ldg(p.bias + r);
+            static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
+          }
+        }
+    __syncwarp();
+    if (lane == 0) p.counters[w_first] = 0u;  // leave the workspace zeroed
   }
 }
 
@@ -478,33 +588,31 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 constexpr int kWarps = W4A16_TMA_WARPS;
 constexpr int kStages = W4A16_TMA_STAGES;
 constexpr int kSlabs = W4A16_TMA_SLABS;
-constexpr int kStageCols = kSlabs * kSlabCols;
+constexpr int kRT = W4A16_TMA_RT;
+constexpr int kTileRows = kMmaRows * kRT;
 
 template <int GS, typename ST>
 constexpr int tma_smem_bytes() {
-  return kWarps * kStages * StageLayout<kSlabs, GS, ST>::kBytes + kWarps * kStages * 8 + 1024;
+  using L = StageLayout<kSlabs, kRT, GS, ST>;
+  return kWarps * kStages * (L::kWStride + L::kSStride + 8) + 1024;
 }
 
-// Split count for a problem: enough items to occupy every warp slot when the
-// layer has few row tiles.
-int choose_split(int ntiles, int nstages, int slots) {
-  if (ntiles * 2 > slots || nstages < 2) return 1;
-  int s = (slots + ntiles - 1) / ntiles;
-  return s < nstages ? s : nstages;
-}
-
-template <int PACK, int GS, typename ST, int NB, typename OT>
-int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, int nsplit, int stages_per_split,
-               const DeviceInfo& di, int dev) {
-  auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs>;
-  constexpr int smem = tma_smem_bytes<GS, ST>();
+template <int PACK, int GS, typename ST, int NB, typename OT, bool XS>
+int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
+  using L = StageLayout<kSlabs, kRT, GS, ST>;
+  auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XS>;
+  const int smem = tma_smem_bytes<GS, ST>() + (XS ? p.K * 2 : 0);
+  if (smem > di.smem_optin) {
+    set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
+    return W4A16_ERR_SHAPE;
+  }
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << dev;
   if (!(configured.load(std::memory_order_acquire) & bit)) {
     const cudaError_t e =
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
     if (e != cudaSuccess) {
-      set_error("cudaFuncSetAttribute(%d bytes): %s", smem, cudaGetErrorString(e));
+      set_error("cudaFuncSetAttribute(%d bytes): %s", di.smem_optin, cudaGetErrorString(e));
       return W4A16_ERR_CUDA;
     }
     configured.fetch_or(bit, std::memory_order_acq_rel);
@@ -516,15 +624,15 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, int nsplit
     return W4A16_ERR_CUDA;
   }
   CUtensorMap wmap, smap;
-  {
-    const cuuint64_t dims[2] = {(cuuint64_t)(p.K / 2), (cuuint64_t)p.N};
-    const cuuint64_t strides[1] = {(cuuint64_t)(p.K / 2)};
-    const cuuint32_t box[2] = {128, kTileRows};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(p.packed),
-                           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  {  // 3-D view {128 bytes, K/256 slabs, N rows}: one box [rows][SLABS][128 B] per window
+    const cuuint64_t dims[3] = {128, (cuuint64_t)(p.K / kSlabCols), (cuuint64_t)p.N};
+    const cuuint64_t strides[2] = {128, (cuuint64_t)(p.K / 2)};
+    const cuuint32_t box[3] = {128, (cuuint32_t)kSlabs, (cuuint32_t)kTileRows};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(p.packed), dims, strides,
+            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled(weights) failed: %d", (int)r);
       return W4A16_ERR_CUDA;
@@ -534,13 +642,13 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, int nsplit
     const int ng = p.K / GS;
     const cuuint64_t dims[2] = {(cuuint64_t)ng, (cuuint64_t)p.N};
     const cuuint64_t strides[1] = {(cuuint64_t)ng * sizeof(ST)};
-    const cuuint32_t box[2] = {(cuuint32_t)StageLayout<kSlabs, GS, ST>::kGroups, kTileRows};
+    const cuuint32_t box[2] = {(cuuint32_t)L::kGroups, (cuuint32_t)kTileRows};
     const cuuint32_t estr[2] = {1, 1};
     const CUtensorMapDataType dt =
         sizeof(ST) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const CUresult r = enc(&smap, dt, 2, const_cast<void*>(p.scale), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    r = enc(&smap, dt, 2, const_cast<void*>(p.scale), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled(scales) failed: %d", (int)r);
       return W4A16_ERR_CUDA;
@@ -558,20 +666,26 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, int nsplit
   prm.N = p.N;
   prm.K = p.K;
   prm.ntiles = (p.N + kTileRows - 1) / kTileRows;
-  prm.nstages = (p.K + kStageCols - 1) / kStageCols;
-  prm.nsplit = nsplit;
-  prm.stages_per_split = stages_per_split;
-  prm.n_items = prm.ntiles * nsplit;
+  prm.kslabs = p.K / kSlabCols;
+  prm.nwin = (prm.kslabs + kSlabs - 1) / kSlabs;
+  prm.units = (long long)prm.ntiles * prm.nwin;
+  const long long slots = (long long)di.sms * kWarps;
+  // Stream-K (equal slab ranges, shared tiles reduced through the workspace) when a
+  // big enough workspace is given; otherwise each warp owns whole tiles.
+  const long long tk = prm.units < slots ? prm.units : slots;
+  const size_t need = kCounterBytes + (size_t)tk * 2 * M * kTileRows * 4;
+  const bool streamk = p.split_k != 1 && tk <= kMaxWarps && p.workspace &&
+                       p.workspace_bytes >= need && aligned(p.workspace, 256);
+  prm.aligned = streamk ? 0 : 1;
+  prm.nwarps = (int)(streamk ? tk : (prm.ntiles < slots ? prm.ntiles : slots));
   prm.partial = nullptr;
   prm.counters = nullptr;
-  if (nsplit > 1) {
+  if (streamk) {
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
     prm.counters = reinterpret_cast<unsigned*>(ws);
     prm.partial = reinterpret_cast<float*>(ws + kCounterBytes);
   }
-  int grid = (prm.n_items + kWarps - 1) / kWarps;
-  if (prm.n_items >= di.sms) grid = di.sms;
-  if (grid > di.sms) grid = di.sms;
+  int grid = prm.nwarps < di.sms ? prm.nwarps : di.sms;
   if (grid < 1) grid = 1;
   kernel<<<grid, kWarps * 32, smem, p.stream>>>(wmap, smap, prm);
   return check_launch("k_gemv_tma");
@@ -594,8 +708,9 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
   // The simple packing (the reference's ladder kernels) only ever carries per-row
   // fp32 scales and fp32 outputs there; other combinations take the generic kernel.
   constexpr bool kTmaVariant =
-      PACK == W4A16_PACK_INTERLEAVED ||
-      (GS == 0 && std::is_same<ST, float>::value && std::is_same<OT, float>::value);
+      (PACK == W4A16_PACK_INTERLEAVED ||
+       (GS == 0 && std::is_same<ST, float>::value && std::is_same<OT, float>::value)) &&
+      StageLayout<kSlabs, kRT, GS, ST>::kScaleBoxOk;
   if constexpr (!kTmaVariant) {
     (void)use_tma;
     (void)di;
@@ -603,35 +718,14 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
     return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
   } else {
   if (!use_tma) return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
-  const int ntiles = (p.N + kTileRows - 1) / kTileRows;
-  const int nstages = (p.K + kStageCols - 1) / kStageCols;
-  int nsplit = 1;
-  if (p.split_k == 0) {
-    nsplit = ntiles <= kMaxSplitTiles ? choose_split(ntiles, nstages, di.sms * kWarps) : 1;
-  } else {
-    nsplit = p.split_k < nstages ? p.split_k : nstages;
-    if (ntiles > kMaxSplitTiles) nsplit = 1;
+  if (M == 1) {
+    // one activation vector: keep it in shared memory when it fits beside the ring
+    if (tma_smem_bytes<GS, ST>() + p.K * 2 <= di.smem_optin)
+      return launch_tma<PACK, GS, ST, 1, OT, true>(p, x, M, y, di, dev);
+    return launch_tma<PACK, GS, ST, 1, OT, false>(p, x, M, y, di, dev);
   }
-  int sps = nstages;
-  if (nsplit > 1) {
-    sps = (nstages + nsplit - 1) / nsplit;
-    nsplit = (nstages + sps - 1) / sps;
-  }
-  if (nsplit > 1) {
-    const size_t need = kCounterBytes + (size_t)nsplit * M * p.N * 4;
-    if (!p.workspace || p.workspace_bytes < need || !aligned(p.workspace, 256)) {
-      if (p.split_k > 1) {
-        set_error("split-K %d needs a 256-byte aligned workspace of %zu bytes (got %zu)",
-                  p.split_k, need, p.workspace_bytes);
-        return W4A16_ERR_WORKSPACE;
-      }
-      nsplit = 1;
-      sps = nstages;
-    }
-  }
-  if (M == 1) return launch_tma<PACK, GS, ST, 1, OT>(p, x, M, y, nsplit, sps, di, dev);
-  if (M <= 8) return launch_tma<PACK, GS, ST, 8, OT>(p, x, M, y, nsplit, sps, di, dev);
-  return launch_tma<PACK, GS, ST, 16, OT>(p, x, M, y, nsplit, sps, di, dev);
+  if (M <= 8) return launch_tma<PACK, GS, ST, 8, OT, false>(p, x, M, y, di, dev);
+  return launch_tma<PACK, GS, ST, 16, OT, false>(p, x, M, y, di, dev);
   }
 }
 
@@ -664,8 +758,7 @@ size_t gemv_counter_bytes() { return kCounterBytes; }
 size_t gemv_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int mc = M < kMaxBatchPerPass ? M : kMaxBatchPerPass;
-  const size_t nstages = (size_t)(K + kStageCols - 1) / kStageCols;
-  return kCounterBytes + nstages * (size_t)mc * N * 4;
+  return kCounterBytes + (size_t)kMaxWarps * 2 * mc * kTileRows * 4;
 }
 
 int launch_gemv(const GemvProblem& p) {

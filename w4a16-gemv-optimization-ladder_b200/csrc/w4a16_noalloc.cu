@@ -4,10 +4,11 @@
 // give it any other device memory: a runtime that plans all device memory at
 // start-up and forbids allocation afterwards (cudaMalloc may synchronise the whole
 // device and breaks such a plan), or a plugin interface whose op signature has no
-// workspace argument.  Layers with few rows still need scratch memory for split-K
-// (per-tile counters plus fp32 partial sums).  This entry point takes that scratch
-// from a fixed array that lives in the library itself, so it calls no cudaMalloc,
-// cudaFree or any allocating routine.
+// workspace argument.  The GEMV still needs scratch memory to balance its work
+// across warps (per-warp counters plus fp32 partial sums of the tiles that
+// neighbouring warps share; about 0.5 MiB for one activation vector, whatever the
+// matrix size).  This entry point takes that scratch from a fixed array that lives
+// in the library itself, so it calls no cudaMalloc, cudaFree or allocating routine.
 //
 // The array (kNoAllocScratchBytes, 4 MiB) is a file-scope __device__ variable: every
 // GPU that loads the library holds one copy until the process exits.  Every call on
@@ -90,8 +91,7 @@ extern "C" int w4a16_gemv_noalloc(const uint8_t* packed, const void* scale, int 
   if (need > kNoAllocScratchBytes) {
     w4a16::set_error(
         "w4a16_gemv_noalloc: rows=%d cols=%d needs %zu bytes of scratch, more than the %zu-byte "
-        "static array (limit: 16384 + 4*rows*ceil(cols/1024) bytes); use w4a16_gemv with a "
-        "workspace",
+        "static array; use w4a16_gemv with a workspace",
         rows, cols, need, kNoAllocScratchBytes);
     return W4A16_ERR_WORKSPACE;
   }
