@@ -103,6 +103,19 @@ struct StageLayout {
   static constexpr bool kScaleBoxOk = !GS || (kGroups * sizeof(ST)) % 16 == 0;
 };
 
+// Shared-memory plan of one CTA (offsets from the 1024-byte aligned base):
+//   [W rings: WARPS x STAGES x kWStride][scale rings: WARPS x STAGES x kSStride]
+//   [mbarriers: WARPS x STAGES x 8][staged activation at a 128-byte boundary]
+template <int WARPS, int STAGES, typename L>
+struct SmemPlan {
+  static constexpr int kScaleOff = WARPS * STAGES * L::kWStride;
+  static constexpr int kBarOff = kScaleOff + WARPS * STAGES * L::kSStride;
+  static constexpr int kXOff = (kBarOff + WARPS * STAGES * 8 + 127) / 128 * 128;
+  // dynamic bytes requested: the plan plus slack for aligning the base to 1024
+  static constexpr int kBytes = kXOff + 1024;
+  static_assert(kScaleOff % 1024 == 0 && kBarOff % 16 == 0 && kXOff % 128 == 0, "smem alignment");
+};
+
 // Byte offset of logical 16-byte chunk c of (row r, slab sl) inside a stage.  The
 // 128-byte swizzle puts chunk c of 128-byte smem line L at c ^ (L & 7), L = 4r + sl:
 // rows g and g+8 of one MMA get the same XOR, and the two rows a quarter-warp reads
@@ -137,11 +150,32 @@ __device__ __forceinline__ uint32_t xs_offset(int col) {
   return (uint32_t)(((grp * 4 + ((off & 31) >> 3)) * 4 + (off >> 5)) * 16);
 }
 
+// Lane part of the weight-fragment offsets: for chunk c = gh*4 + t of slab sl in row
+// r = g (row g + 8 adds 8 lines = 4096 bytes, rt adds 16 rows), the swizzled offset
+// w_offset<4>(g, sl, c) depends only on the lane and (gh, sl): computed once.
+struct LaneOffsets {
+  uint32_t w[2][4];  // [gh][sl]
+  uint32_t x;        // t * 16 (fragment order of the staged activation)
+};
+
+__device__ __forceinline__ LaneOffsets lane_offsets(int g, int t) {
+  LaneOffsets o;
+#pragma unroll
+  for (int gh = 0; gh < 2; ++gh)
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) o.w[gh][sl] = w_offset<4>(g, sl, gh * 4 + t);
+  o.x = (uint32_t)t * 16u;
+  return o;
+}
+
 template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS>
 __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, uint32_t xs,
                                                int nslab, int kcol0, const TmaParams& p, int g,
-                                               int t, float (&acc)[RT][2][BatchCfg<NB>::kHalves][4],
+                                               int t, const LaneOffsets& lo,
+                                               float (&acc)[RT][2][BatchCfg<NB>::kHalves][4],
                                                float (&tot)[RT][BatchCfg<NB>::kHalves][4]) {
+  // activation fragments of this window: 16 bytes at xwin + ((sl*2 + gh)*4 + j)*64
+  const uint32_t xwin = xs + lo.x + (uint32_t)(kcol0 >> 7) * 256u;
   constexpr int NH = BatchCfg<NB>::kHalves;
   constexpr int kGroups = SLABS * 2;
 #pragma unroll
@@ -154,8 +188,9 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
 #pragma unroll
         for (int gh = 0; gh < 2; ++gh) {
           const int c = gh * 4 + t;
-          wa[rt][gh] = lds128(wbase + w_offset<SLABS>(rt * 16 + g, sl, c));
-          wb[rt][gh] = lds128(wbase + w_offset<SLABS>(rt * 16 + g + 8, sl, c));
+          (void)c;
+          wa[rt][gh] = lds128(wbase + lo.w[gh][sl] + rt * 16 * SLABS * 128);
+          wb[rt][gh] = lds128(wbase + lo.w[gh][sl] + rt * 16 * SLABS * 128 + 8 * SLABS * 128);
         }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -165,7 +200,8 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
           uint4 xv[NH];
 #pragma unroll
           for (int h = 0; h < NH; ++h) {
-            xv[h] = XS ? lds128(xs + xs_offset(col)) : load_x<NB>(p.x, p.K, p.M, g, h, col);
+            xv[h] = XS ? lds128(xwin + ((sl * 2 + gh) * 4 + j) * 64)
+                       : load_x<NB>(p.x, p.K, p.M, g, h, col);
             if (PACK == W4A16_PACK_SIMPLE) xv[h] = simple_order(xv[h]);
           }
 #pragma unroll
@@ -240,7 +276,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   // XS: the CTA first copies the activation vector into shared memory (fragment
   // order, see xs_offset); every B fragment is then one shared-memory load.
-  const uint32_t xs = base + (uint32_t)(WARPS * STAGES * (L::kWStride + L::kSStride + 8));
+  using Plan = SmemPlan<WARPS, STAGES, L>;
+  const uint32_t xs = base + (uint32_t)Plan::kXOff;
   if (XS) {
     uint8_t* xsp = smem_raw + (xs - smem_addr(smem_raw));
     for (int c = threadIdx.x; c < (p.K >> 3); c += blockDim.x)
@@ -268,8 +305,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int count = (int)(u1 - u0);
 
   const uint32_t wring = base + (uint32_t)(warp * STAGES * L::kWStride);
-  const uint32_t sring = base + (uint32_t)(WARPS * STAGES * L::kWStride + warp * STAGES * L::kSStride);
-  const uint32_t bar0 = base + (uint32_t)(WARPS * STAGES * (L::kWStride + L::kSStride) + warp * STAGES * 8);
+  const uint32_t sring = base + (uint32_t)(Plan::kScaleOff + warp * STAGES * L::kSStride);
+  const uint32_t bar0 = base + (uint32_t)(Plan::kBarOff + warp * STAGES * 8);
 
   if (lane == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(bar0 + 8 * s, 1);
@@ -279,6 +316,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
   __syncwarp();
   const uint64_t policy = l2_policy_evict_first();
+  const LaneOffsets lo = lane_offsets(g, t);
 
   // Producer position (identical in every lane; lane 0 issues the copies).
   int p_tile = first_tile, p_win = first_win;
@@ -349,10 +387,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int nslab = min(SLABS, ks - s0);
     if (nslab == SLABS)
       consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS>(wbase, sbase, xs, nslab, s0 * kSlabCols,
-                                                            p, g, t, acc, tot);
+                                                            p, g, t, lo, acc, tot);
     else
       consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS>(wbase, sbase, xs, nslab, s0 * kSlabCols,
-                                                             p, g, t, acc, tot);
+                                                             p, g, t, lo, acc, tot);
     __syncwarp();  // every lane has read the slot before it is refilled
     issue_one();
 
@@ -594,7 +632,7 @@ constexpr int kTileRows = kMmaRows * kRT;
 template <int GS, typename ST>
 constexpr int tma_smem_bytes() {
   using L = StageLayout<kSlabs, kRT, GS, ST>;
-  return kWarps * kStages * (L::kWStride + L::kSStride + 8) + 1024;
+  return SmemPlan<kWarps, kStages, L>::kBytes;
 }
 
 template <int PACK, int GS, typename ST, int NB, typename OT, bool XS>
