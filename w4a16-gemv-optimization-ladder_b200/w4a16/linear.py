@@ -60,15 +60,21 @@ class W4A16Linear(nn.Module):
         return y.to(x.dtype).view(*lead, self.out_features)
 
 
-def replace_linear_with_w4a16(module, group=0, keep_dense=True, scale_dtype=torch.float32):
+def replace_linear_with_w4a16(module, group=0, keep_dense=True, scale_dtype=torch.float32,
+                              device=None):
     """Swap every nn.Linear under `module` for a W4A16Linear (reference kernels.py:127-137).
 
     Defaults match the reference: per-row scales, the dense fp16 weight kept for large
-    batches.  group=128 uses group-wise scales; keep_dense=False drops the dense copy."""
+    batches, buffers on the GPU.  group=128 uses group-wise scales; keep_dense=False
+    drops the dense copy; device places the buffers (default: the weight's CUDA
+    device, else the current one)."""
     for name, child in module.named_children():
         if isinstance(child, nn.Linear):
             w = child.weight.data
-            dev = w.device if w.is_cuda else torch.device("cuda", torch.cuda.current_device())
+            if device is not None:
+                dev = torch.device(device)
+            else:
+                dev = w.device if w.is_cuda else torch.device("cuda", torch.cuda.current_device())
             if group:
                 q, scale = quantize_int4_group(w.float(), group=group)
             else:
@@ -77,5 +83,6 @@ def replace_linear_with_w4a16(module, group=0, keep_dense=True, scale_dtype=torc
             dense = w.half().to(dev) if keep_dense else None
             setattr(module, name, W4A16Linear(dense, child.bias, packed, scale.to(scale_dtype).to(dev)))
         else:
-            replace_linear_with_w4a16(child, group=group, keep_dense=keep_dense, scale_dtype=scale_dtype)
+            replace_linear_with_w4a16(child, group=group, keep_dense=keep_dense,
+                                      scale_dtype=scale_dtype, device=device)
     return module
