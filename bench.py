@@ -57,6 +57,7 @@ class ClockSampler(threading.Thread):
         self.period = period
         self.samples = []
         self.sm_max = None
+        self.power_limit = None
         self.error = None
         self._halt = threading.Event()
         self._handle = None
@@ -70,6 +71,10 @@ class ClockSampler(threading.Thread):
             except Exception:
                 self._handle = pynvml.nvmlDeviceGetHandleByIndex(device)
             self.sm_max = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            try:
+                self.power_limit = pynvml.nvmlDeviceGetEnforcedPowerLimit(self._handle) / 1000.0
+            except Exception:
+                self.power_limit = None
             self._nvml = pynvml
         except Exception as e:  # NVML missing: report it, keep benchmarking
             self.error = str(e)
@@ -85,7 +90,9 @@ class ClockSampler(threading.Thread):
                     r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
                 except AttributeError:
                     r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._handle)
-                self.samples.append((sm, r))
+                mem = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_MEM)
+                pw = nv.nvmlDeviceGetPowerUsage(self._handle) / 1000.0
+                self.samples.append((sm, r, mem, pw))
             except Exception as e:
                 self.error = str(e)
                 return
@@ -100,11 +107,16 @@ class ClockSampler(threading.Thread):
             return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": [],
                     "note": self.error or "no samples"}
         reasons = set()
-        for _, r in self.samples:
+        for _, r, _, _ in self.samples:
             for bit, name in _REASONS.items():
                 if r & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.sm_max,
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": self.sm_max,
+                "sm_mhz_min": min(s[0] for s in self.samples),
+                "mem_mhz": statistics.median(s[2] for s in self.samples),
+                "power_w_median": round(statistics.median(s[3] for s in self.samples), 1),
+                "power_w_max": round(max(s[3] for s in self.samples), 1),
+                "power_limit_w": self.power_limit,
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
@@ -422,7 +434,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -67,11 +67,15 @@ __device__ __forceinline__ void record_device_error(int code) { atomicCAS(&g_dev
 constexpr int kMmaRows = 16;      // rows of one m16n8k16 A fragment
 constexpr int kSlabCols = 256;    // columns per 128-byte slab of a packed row
 constexpr int kMaxBatchPerPass = 16;
-// Stream-K workspace layout: [per-warp counters: kMaxWarps x u32][fp32 partials:
-// kMaxWarps x 2 slots x batch x tile rows].  Both regions have a size fixed by
-// kMaxWarps, not by the problem, so calls of any shape can share one workspace.
+// Workspace layout: [counters: kMaxWarps x u32][fp32 partials: kMaxWarps x 2 slots x
+// batch x tile rows].  Counter w (< kMaxWarps - 2) belongs to the stream-K tile whose
+// first unit warp w owns; the last two are the dynamic scheduler's next-tile and
+// finished-warp counters.  Both regions have a size fixed by kMaxWarps, not by the
+// problem, so calls of any shape can share one workspace.
 constexpr int kMaxWarps = 4096;
 constexpr size_t kCounterBytes = (size_t)kMaxWarps * 4;
+constexpr int kNextTileCounter = kMaxWarps - 1;
+constexpr int kDoneWarpCounter = kMaxWarps - 2;
 
 struct TmaParams {
   const void* scale_rows;  // per-row scale [N] (group 0)
@@ -84,8 +88,18 @@ struct TmaParams {
   int M, N, K;
   int ntiles, kslabs, nwin;
   int nwarps;              // warps that receive work
-  int aligned;             // 1: each warp owns whole tiles (no workspace needed)
+  int sched;               // kSchedStreamK, kSchedStatic or kSchedDynamic
 };
+
+// Work distribution over (16-row tile, 1024-column window) units:
+//   kSchedStreamK  every warp takes an equal contiguous range of units; tiles shared
+//                  by neighbouring warps are reduced through the workspace.  Best when
+//                  there are few tiles with many windows (short, wide layers).
+//   kSchedStatic   every warp takes an equal contiguous range of whole tiles (no
+//                  workspace needed).
+//   kSchedDynamic  warps pull whole tiles from an atomic counter in the workspace, so
+//                  SMs that stream faster take more tiles.  Best for many tiles.
+enum Sched : int { kSchedStreamK = 0, kSchedStatic = 1, kSchedDynamic = 2 };
 
 // Shared-memory stage of one warp: a window of SLABS 256-column slabs of RT*16 rows,
 // one 3-D TMA box laid out [row][slab][128 B] with the 128-byte swizzle (1024-byte
@@ -291,15 +305,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int nwin = p.nwin;
   const long long U = p.units;
   const int T = p.nwarps;
+  const bool dyn = p.sched == kSchedDynamic;
+  unsigned* next_tile = p.counters + kNextTileCounter;
+  auto pull_tile = [&]() -> int {  // dynamic scheduling: the next unclaimed tile
+    unsigned v = 0;
+    if (lane == 0) v = atomicAdd(next_tile, 1u);
+    return (int)__shfl_sync(0xffffffffu, v, 0);
+  };
   long long u0, u1;
-  if (p.aligned) {
+  if (p.sched == kSchedStatic) {
     u0 = (long long)gw * p.ntiles / T * nwin;
     u1 = (long long)(gw + 1) * p.ntiles / T * nwin;
-  } else {
+  } else if (p.sched == kSchedStreamK) {
     u0 = (long long)gw * U / T;
     u1 = (long long)(gw + 1) * U / T;
+  } else {
+    u0 = (long long)pull_tile() * nwin;
+    u1 = u0 < U ? U : u0;  // bounded below by the tiles actually pulled
   }
-  if (u0 >= u1) return;
   const int first_tile = (int)(u0 / nwin);
   const int first_win = (int)(u0 - (long long)first_tile * nwin);
   const int count = (int)(u1 - u0);
@@ -318,11 +341,21 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const uint64_t policy = l2_policy_evict_first();
   const LaneOffsets lo = lane_offsets(g, t);
 
-  // Producer position (identical in every lane; lane 0 issues the copies).
+  // Producer position (identical in every lane; lane 0 issues the copies).  Under
+  // dynamic scheduling slot_tile remembers which tile each ring slot was filled from.
   int p_tile = first_tile, p_win = first_win;
   int issued = 0;
+  bool p_done = count <= 0;
+  int slot_tile[STAGES];
+#pragma unroll
+  for (int i = 0; i < STAGES; ++i) slot_tile[i] = first_tile;
   auto issue_one = [&]() {
-    if (issued >= count) return;
+    if (issued >= count || p_done) return;
+    if (dyn) {
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i)
+        if ((uint32_t)issued % STAGES == (uint32_t)i) slot_tile[i] = p_tile;
+    }
     const uint32_t slot = (uint32_t)issued % STAGES;
     if (lane == 0) {
       const int row0 = p_tile * kRows;
@@ -337,7 +370,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     ++issued;
     if (++p_win == nwin) {
       p_win = 0;
-      ++p_tile;
+      p_tile = dyn ? pull_tile() : p_tile + 1;
+      if (dyn && p_tile >= p.ntiles) p_done = true;
     }
   };
 
@@ -351,6 +385,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
 #pragma unroll 1
   for (int consumed = 0; consumed < count; ++consumed) {
+    if (dyn) {
+      if (consumed >= issued) break;  // the producer has run out of tiles
+#pragma unroll
+      for (int i = 0; i < STAGES; ++i)
+        if ((uint32_t)consumed % STAGES == (uint32_t)i) tile = slot_tile[i];
+    }
     if (win == 0 || consumed == 0) {  // a tile starts in this warp's range
       tile_w0 = win;
 #pragma unroll
@@ -400,7 +440,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       win = 0;
       ++tile;
     }
-    if (!tile_done && consumed + 1 < count) continue;  // the tile goes on in this warp
+    if (!tile_done && (dyn || consumed + 1 < count)) continue;  // the tile goes on here
 
     // ---- tile epilogue
     if (!GS) {
@@ -483,6 +523,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         }
     __syncwarp();
     if (lane == 0) p.counters[w_first] = 0u;  // leave the workspace zeroed
+  }
+  if (dyn && lane == 0) {
+    // Every warp has made its last pull before it counts itself done, so the last
+    // one can rewind the tile counter for the next call.
+    if (atomicAdd(p.counters + kDoneWarpCounter, 1u) == (unsigned)(T - 1)) {
+      *next_tile = 0u;
+      p.counters[kDoneWarpCounter] = 0u;
+    }
   }
 }
 
@@ -708,17 +756,21 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   prm.nwin = (prm.kslabs + kSlabs - 1) / kSlabs;
   prm.units = (long long)prm.ntiles * prm.nwin;
   const long long slots = (long long)di.sms * kWarps;
-  // Stream-K (equal slab ranges, shared tiles reduced through the workspace) when a
-  // big enough workspace is given; otherwise each warp owns whole tiles.
-  const long long tk = prm.units < slots ? prm.units : slots;
+  const long long tk = prm.units < slots ? prm.units : slots;           // stream-K warps
+  const long long tt = prm.ntiles < slots ? prm.ntiles : slots;         // whole-tile warps
   const size_t need = kCounterBytes + (size_t)tk * 2 * M * kTileRows * 4;
-  const bool streamk = p.split_k != 1 && tk <= kMaxWarps && p.workspace &&
+  const bool have_ws = p.split_k != 1 && tk <= kMaxWarps - 2 && p.workspace &&
                        p.workspace_bytes >= need && aligned(p.workspace, 256);
-  prm.aligned = streamk ? 0 : 1;
-  prm.nwarps = (int)(streamk ? tk : (prm.ntiles < slots ? prm.ntiles : slots));
+  if (!have_ws)
+    prm.sched = kSchedStatic;
+  else if (prm.ntiles * 4 >= slots || prm.nwin <= 2)
+    prm.sched = kSchedDynamic;
+  else
+    prm.sched = kSchedStreamK;
+  prm.nwarps = (int)(prm.sched == kSchedStreamK ? tk : tt);
   prm.partial = nullptr;
   prm.counters = nullptr;
-  if (streamk) {
+  if (have_ws) {
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
     prm.counters = reinterpret_cast<unsigned*>(ws);
     prm.partial = reinterpret_cast<float*>(ws + kCounterBytes);
