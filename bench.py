@@ -330,6 +330,9 @@ def run_ours(args, rank, world, dev):
         del prow
         torch.cuda.empty_cache()
 
+    if rank == 0 and not args.no_decode:
+        extras.update(decode_step_times(dev, stream))
+
     # end to end through the public API with host buffers (pinned), copies timed
     packed_h = copies[0][0].cpu().pin_memory()
     scale_h = copies[0][1].cpu().pin_memory()
@@ -391,6 +394,41 @@ def run_ours(args, rank, world, dev):
     return result
 
 
+def decode_step_times(dev, stream, reps=200):
+    """Decode step of the random-init Llama-3.2-1B architecture (16 layers, hidden 2048,
+    GQA 32/8, SwiGLU 8192, vocab 128256, tied head), batch 1, KV length 512, replayed
+    from one CUDA graph: int4 group-128 weights with the fused norm / attention / SwiGLU
+    kernels, the same GEMVs with torch ops in between, and dense fp16 on cuBLAS."""
+    from w4a16.decode import LLAMA_3_2_1B, W4A16LlamaDecoder
+    out = {}
+    variants = (("decode_step_us", False, True), ("decode_step_us_unfused", False, False),
+                ("decode_step_us_fp16_cublas", True, False))
+    for name, dense, fused in variants:
+        dec = W4A16LlamaDecoder(LLAMA_3_2_1B, device=dev, seed=0, dense=dense, fused=fused)
+        dec.fill_cache(LLAMA_3_2_1B.max_len - 1)
+        dec.capture()
+        dec.token.fill_(1)
+        dec.pos.fill_(LLAMA_3_2_1B.max_len - 1)
+        for _ in range(10):
+            dec.graph.replay()
+        torch.cuda.synchronize()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record(stream)
+        for _ in range(reps):
+            dec.graph.replay()
+        en.record(stream)
+        torch.cuda.synchronize()
+        us = st.elapsed_time(en) * 1000.0 / reps
+        out[name] = round(us, 2)
+        if fused:
+            out["decode_weight_bytes"] = dec.weight_bytes()
+            out["decode_weight_gbs"] = round(dec.weight_bytes() / us / 1e3, 1)
+        del dec
+        torch.cuda.empty_cache()
+    out["decode_speedup_vs_fp16"] = round(out["decode_step_us_fp16_cublas"] / out["decode_step_us"], 3)
+    return out
+
+
 def run_reference(args, rank, world):
     """The reference's CPU algorithm (dequant then matmul, fp32) via the C oracle on
     a bounded row sample of the same workload, extrapolated to the full matrix."""
@@ -438,6 +476,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-step measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -50,6 +50,7 @@ enum w4a16_status {
 
 enum w4a16_dtype { W4A16_DTYPE_F32 = 0, W4A16_DTYPE_F16 = 1 };
 enum w4a16_packing { W4A16_PACK_INTERLEAVED = 0, W4A16_PACK_SIMPLE = 1 };
+enum w4a16_prologue { W4A16_PROLOGUE_NONE = 0, W4A16_PROLOGUE_RMSNORM = 1, W4A16_PROLOGUE_SWIGLU = 2 };
 
 /* ---------------------------------------------------------------------------
  * Reference-mirroring entry points: out[r] = sum_k q[r][k] * scale * vec[k], fp32.
@@ -116,6 +117,42 @@ int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_
                const void* x, int batch, int rows, int cols, void* out, int out_dtype,
                const float* bias, void* workspace, size_t workspace_bytes,
                w4a16_stream_t stream);
+
+/* w4a16_gemv with the activation computed inside the kernel, for decode steps of
+ * Llama-style models.  The reference applies these operations as separate torch ops
+ * between its GEMVs (the HF model around W4A16Linear, src/w4a16/kernels.py:113-124);
+ * here they are the prologue of the GEMV that consumes them:
+ *   W4A16_PROLOGUE_RMSNORM  src = fp32 h [cols], gamma = fp32 [cols]:
+ *                           x = fp16(h * rsqrt(mean(h^2) + eps) * gamma)
+ *   W4A16_PROLOGUE_SWIGLU   src = fp16 [2*cols] = gate | up:  x = fp16(silu(gate) * up)
+ * One activation vector; interleaved packing; cols % 256 == 0 and small enough for the
+ * vector to sit in shared memory beside the weight rings (cols <= 10752 with group-128
+ * fp32 scales, <= 16896 with one scale per row).  out (fp32 or fp16 [rows]) may alias bias
+ * (fp32): out = W x + bias is then an in-place residual add.  out must not overlap src. */
+int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, int group,
+                     int prologue, const void* src, const float* gamma, float eps, int rows,
+                     int cols, void* out, int out_dtype, const float* bias, void* workspace,
+                     size_t workspace_bytes, w4a16_stream_t stream);
+
+/* Decode-step attention of a Llama-style layer for one token (batch 1), the kernel
+ * that sits between the QKV and output GEMVs of a decode step.  The reference leaves
+ * this to the Hugging Face model around its swapped Linears (benchmarks/end_to_end.py:
+ * 24-42); here one launch does, at position p = *pos (device int64):
+ *   q, k = rotary(qkv[q], qkv[k]) with rotate-half tables cos_t/sin_t (fp32 [max_len][64])
+ *   k_cache[kvh][p] = fp16(k), v_cache[kvh][p] = qkv[v]          (fp16 [kv_heads][max_len][64])
+ *   out[h] = softmax(q_h . k_cache[kvh(h)][0..p] / 8) @ v_cache[kvh(h)][0..p]   (fp16 [heads*64])
+ * qkv = fp16 [(heads + 2*kv_heads) * 64] laid out q | k | v; head_dim must be 64 and
+ * heads / kv_heads <= 32.  Positions are split over `splits` CTAs per kv head whose
+ * fp32 partial softmaxes are combined by the last one; scratch is a zero-filled device
+ * buffer of w4a16_decode_attention_scratch_bytes(heads, kv_heads, splits) bytes that the
+ * kernel leaves zeroed.  A position outside [0, max_len) writes nothing to the caches and
+ * NaN to out.  Calls sharing a scratch buffer must be ordered on one stream. */
+int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
+                           const int64_t* pos, void* k_cache, void* v_cache, void* out,
+                           void* scratch, size_t scratch_bytes, int heads, int kv_heads,
+                           int head_dim, int max_len, int splits, w4a16_stream_t stream);
+
+size_t w4a16_decode_attention_scratch_bytes(int heads, int kv_heads, int splits);
 
 /* Bytes of workspace that let w4a16_gemv balance its work across warps (stream-K)
  * for this batch size; independent of rows and cols (about 0.5 MiB per activation

@@ -102,3 +102,46 @@ def test_python_ops_fail_loudly_without_library(monkeypatch, tmp_path):
     finally:
         monkeypatch.delenv(_lib.ENV_LIB)
         _lib.lib.cache_clear()
+
+
+def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0):
+    return lib.w4a16_gemv_fused(ctypes.c_void_p(1 << 12), ctypes.c_void_p(1 << 12), 0, 0, prologue,
+                                ctypes.c_void_p(src), ctypes.c_void_p(gamma), 1e-5, rows, cols,
+                                ctypes.c_void_p(out), odt, None, None, 0, None)
+
+
+def test_fused_gemv_host_validation(lib):
+    assert _fused(lib, prologue=0) == -4                 # only the RMSNorm / SwiGLU prologues
+    assert _fused(lib, prologue=7) == -4
+    assert _fused(lib, src=0) == -1
+    assert _fused(lib, gamma=0) == -1                    # RMSNorm needs gamma
+    assert _fused(lib, gamma=(1 << 20) + 4) == -3
+    assert _fused(lib, out=(1 << 16) + 512) == -2        # out inside src (fp32 [256] = 1 KiB)
+    assert b"overlaps" in lib.w4a16_last_error_string()
+    assert _fused(lib, out=(1 << 16) - 32) == -2         # out [16] fp32 runs into src
+    assert _fused(lib, cols=200) == -2
+    assert _fused(lib, rows=0) == 0                      # empty: no-op before any CUDA call
+
+
+def _attn(lib, qkv=1 << 12, pos=1 << 13, scratch=1 << 14, scratch_bytes=1 << 20, heads=32,
+          kv_heads=8, head_dim=64, max_len=512, splits=16):
+    p = ctypes.c_void_p
+    return lib.w4a16_decode_attention(p(qkv), p(1 << 15), p(1 << 15), p(pos), p(1 << 16), p(1 << 17),
+                                      p(1 << 18), p(scratch), scratch_bytes, heads, kv_heads, head_dim,
+                                      max_len, splits, None)
+
+
+def test_decode_attention_host_validation(lib):
+    assert lib.w4a16_decode_attention_scratch_bytes(32, 8, 16) == (32 * 16 * 66 + 8) * 4
+    assert lib.w4a16_decode_attention_scratch_bytes(0, 8, 16) == 0
+    assert _attn(lib, qkv=0) == -1
+    assert _attn(lib, head_dim=128) == -2
+    assert _attn(lib, kv_heads=5) == -2                  # heads % kv_heads
+    assert _attn(lib, heads=64, kv_heads=1) == -2        # more than 32 query heads per kv head
+    assert _attn(lib, splits=0) == -2
+    assert _attn(lib, splits=600) == -2                  # more splits than positions
+    assert _attn(lib, max_len=0) == -2
+    assert _attn(lib, qkv=(1 << 12) + 2) == -3
+    assert _attn(lib, pos=(1 << 13) + 4) == -3
+    assert _attn(lib, scratch_bytes=100) == -5
+    assert b"scratch" in lib.w4a16_last_error_string()

@@ -1,0 +1,65 @@
+"""Decode step of the Llama-architecture model on the W4A16 kernels (GPU).
+
+The graph-replayed step must equal the eager step, and both must match an fp32 torch
+evaluation of the same step from the dequantised weights (the decoder itself rounds the
+GEMV inputs and outputs to fp16, as the reference's fp16 models do)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _small():
+    from w4a16.decode import LlamaDecodeConfig
+
+    return LlamaDecodeConfig(layers=2, vocab=4096, max_len=128)
+
+
+@pytest.mark.parametrize("dense,fused", [(False, True), (False, False), (True, False)])
+def test_eager_step_matches_fp32_reference(dense, fused):
+    from w4a16.decode import W4A16LlamaDecoder
+
+    dec = W4A16LlamaDecoder(_small(), dense=dense, fused=fused, seed=3)
+    dec.fill_cache(63)
+    ref = dec.reference_logits(token=17, pos=63)
+    out = dec.step(token=17, pos=63).clone()
+    err = (out - ref).abs().max().item()
+    assert err <= 2e-2 * ref.abs().max().item(), err
+
+
+def test_graph_replay_equals_eager_and_advances_cache():
+    from w4a16.decode import W4A16LlamaDecoder
+
+    dec = W4A16LlamaDecoder(_small(), seed=4)
+    dec.fill_cache(40)
+    k0 = dec.k_cache.clone()
+    v0 = dec.v_cache.clone()
+    eager = dec.step(token=5, pos=40).clone()
+    k_eager = dec.k_cache[:, :, 40].clone()
+    dec.k_cache.copy_(k0)
+    dec.v_cache.copy_(v0)
+    dec.capture()
+    dec.k_cache.copy_(k0)
+    dec.v_cache.copy_(v0)
+    replay = dec.replay(token=5, pos=40).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(replay, eager)
+    assert torch.equal(dec.k_cache[:, :, 40], k_eager)
+    nxt = dec.replay(token=int(replay.argmax()), pos=41).clone()   # the next position
+    assert torch.isfinite(nxt).all() and not torch.equal(nxt, replay)
+    assert not torch.equal(dec.k_cache[:, :, 41], k0[:, :, 41])
+
+
+def test_full_size_weight_bytes():
+    from w4a16.decode import LLAMA_3_2_1B, W4A16LlamaDecoder
+
+    dec = W4A16LlamaDecoder(LLAMA_3_2_1B, seed=0)
+    # 113 Linears of Llama-3.2-1B (q,k,v,o,gate,up,down x 16 + lm_head) at 0.5 B/weight plus
+    # fp32 group-128 scales (4 B per 128 weights)
+    weights = 16 * (2048 * 3072 + 2048 * 2048 + 2048 * 16384 + 8192 * 2048) + 128256 * 2048
+    assert dec.weight_bytes() == weights // 2 + weights // 128 * 4
+    dec.fill_cache(511)
+    dec.capture()
+    logits = dec.replay(token=1, pos=511)
+    torch.cuda.synchronize()
+    assert torch.isfinite(logits).all()

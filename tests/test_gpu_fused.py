@@ -1,0 +1,205 @@
+"""Decode-step kernels around the GEMV (GPU): the RMSNorm / SwiGLU prologues fused into
+the GEMV, and the rotary + KV-cache write + attention kernel.
+
+The prologues are checked against an fp32 restatement of the activation (numpy) fed to
+the oracle GEMV; the activation is rounded to fp16 on both sides, so a difference can
+only come from an fp16 rounding tie landing the other way (one ulp on a handful of
+elements) and from the GEMV's summation order.  Attention is checked against an fp32
+torch evaluation of rotate-half rotary, the cache update and softmax attention."""
+import numpy as np
+import pytest
+import torch
+
+import w4a16 as K
+from oracle import c_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(rows, cols, group, seed, scale_dtype=torch.float32):
+    torch.manual_seed(seed)
+    w = torch.randn(rows, cols, device="cuda") * 0.02
+    packed, scale = K.quantize_pack(w, group=group, scale_dtype=scale_dtype)
+    return packed, scale, packed.cpu().numpy(), scale.float().cpu().numpy()
+
+
+def _oracle(pk, s, x, group):
+    return c_oracle.gemv(pk, s, x, group=group).astype(np.float64)
+
+
+def _rmsnorm_np(h, gamma, eps):
+    h = h.astype(np.float32)
+    r = np.float32(1.0) / np.sqrt(np.mean(h * h, dtype=np.float32) + np.float32(eps), dtype=np.float32)
+    return (h * r * gamma.astype(np.float32)).astype(np.float16)
+
+
+def _swiglu_np(gu):
+    k = gu.shape[0] // 2
+    g, u = gu[:k].astype(np.float32), gu[k:].astype(np.float32)
+    return (g / (np.float32(1) + np.exp(-g)) * u).astype(np.float16)
+
+
+def _close(got, ref, rel=2e-3):
+    err = np.abs(got.astype(np.float64) - ref)
+    tol = rel * np.abs(ref).max() + 1e-6
+    assert (err <= tol).all(), (err.max(), tol)
+
+
+@pytest.mark.parametrize("rows,cols,group", [(3072, 2048, 128), (16384, 2048, 128), (128256, 2048, 128),
+                                             (300, 512, 0), (4096, 8192, 128)])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_gemv_rmsnorm_matches_oracle(rows, cols, group, out_dtype):
+    packed, scale, pk, s = _weights(rows, cols, group, seed=rows + cols)
+    torch.manual_seed(7)
+    h = torch.randn(cols, device="cuda") * 3.0
+    gamma = torch.rand(cols, device="cuda") + 0.5
+    y = K.gemv_rmsnorm(packed, scale, h, gamma, 1e-5, group=group, out_dtype=out_dtype)
+    assert y.dtype == out_dtype and y.shape == (rows,)
+    x = _rmsnorm_np(h.cpu().numpy(), gamma.cpu().numpy(), 1e-5)
+    ref = _oracle(pk, s, x, group)
+    _close(y.float().cpu().numpy(), ref, rel=2e-3 if out_dtype == torch.float32 else 4e-3)
+
+
+@pytest.mark.parametrize("rows,cols,group", [(2048, 8192, 128), (2048, 2048, 0), (512, 10752, 128)])  # 10752: the longest group-128 vector that fits
+def test_gemv_swiglu_matches_oracle(rows, cols, group):
+    packed, scale, pk, s = _weights(rows, cols, group, seed=3 * rows + cols)
+    torch.manual_seed(8)
+    gu = (torch.randn(2 * cols, device="cuda") * 2.0).half()
+    y = K.gemv_swiglu(packed, scale, gu, group=group)
+    ref = _oracle(pk, s, _swiglu_np(gu.cpu().numpy()), group)
+    _close(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("split_k", [True, False])
+def test_fused_in_place_residual(split_k):
+    # h += W_down swiglu(gu) with out aliasing bias, as the decode step does
+    rows, cols = 2048, 8192
+    packed, scale, pk, s = _weights(rows, cols, 128, seed=11)
+    torch.manual_seed(9)
+    gu = torch.randn(2 * cols, device="cuda").half()
+    h = torch.randn(rows, device="cuda")
+    h0 = h.cpu().numpy().astype(np.float64)
+    out = K.gemv_swiglu(packed, scale, gu, group=128, bias=h, out=h, split_k=split_k)
+    assert out.data_ptr() == h.data_ptr()
+    ref = h0 + _oracle(pk, s, _swiglu_np(gu.cpu().numpy()), 128)
+    _close(h.cpu().numpy(), ref)
+    # RMSNorm prologue with an in-place residual on a different vector
+    packed2, scale2, pk2, s2 = _weights(cols, rows, 128, seed=12)
+    acc = torch.randn(cols, device="cuda")
+    acc0 = acc.cpu().numpy().astype(np.float64)
+    gamma = torch.ones(rows, device="cuda")
+    K.gemv_rmsnorm(packed2, scale2, h, gamma, group=128, bias=acc, out=acc, split_k=split_k)
+    ref2 = acc0 + _oracle(pk2, s2, _rmsnorm_np(h.cpu().numpy(), gamma.cpu().numpy(), 1e-5), 128)
+    _close(acc.cpu().numpy(), ref2)
+
+
+def test_fused_fp16_scales_and_determinism():
+    packed, scale, pk, s = _weights(8192, 2048, 128, seed=13, scale_dtype=torch.float16)
+    h = torch.randn(2048, device="cuda")
+    gamma = torch.rand(2048, device="cuda")
+    a = K.gemv_rmsnorm(packed, scale, h, gamma, group=128)
+    b = K.gemv_rmsnorm(packed, scale, h, gamma, group=128)
+    assert torch.equal(a, b)
+    _close(a.cpu().numpy(), _oracle(pk, s, _rmsnorm_np(h.cpu().numpy(), gamma.cpu().numpy(), 1e-5), 128))
+
+
+def test_fused_rejects_unsupported_shapes():
+    packed, scale, _, _ = _weights(64, 384, 128, seed=14)         # cols % 256 != 0
+    with pytest.raises(RuntimeError, match="256"):
+        K.gemv_rmsnorm(packed, scale, torch.randn(384, device="cuda"), torch.ones(384, device="cuda"),
+                       group=128)
+    packed, scale, _, _ = _weights(16, 131072, 128, seed=15)      # vector too long for shared memory
+    with pytest.raises(RuntimeError, match="cols <="):
+        K.gemv_swiglu(packed, scale, torch.randn(2 * 131072, device="cuda").half(), group=128)
+    packed, scale, _, _ = _weights(256, 256, 128, seed=16)
+    src = torch.randn(512, device="cuda")
+    with pytest.raises(RuntimeError, match="overlaps"):           # out overlaps the source vector
+        K.gemv_rmsnorm(packed, scale, src[:256], torch.ones(256, device="cuda"), group=128, out=src[128:384])
+
+
+# --------------------------------------------------------------------- attention
+
+def _rope_tables(max_len, theta=500000.0, D=64):
+    inv = 1.0 / (theta ** (torch.arange(0, D, 2, device="cuda").float() / D))
+    ang = torch.arange(max_len, device="cuda").float()[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.cos()], 1).contiguous(), torch.cat([ang.sin(), ang.sin()], 1).contiguous()
+
+
+def _attention_ref(qkv, cos, sin, pos, kc, vc, heads, kv_heads):
+    D = 64
+    x = qkv.float()
+    q = x[: heads * D].view(heads, D)
+    k = x[heads * D:(heads + kv_heads) * D].view(kv_heads, D)
+    v = x[(heads + kv_heads) * D:].view(kv_heads, D)
+
+    def rope(t):
+        rot = torch.cat([-t[:, D // 2:], t[:, : D // 2]], 1)
+        return t * cos[pos] + rot * sin[pos]
+
+    q, k = rope(q), rope(k)
+    kc, vc = kc.float().clone(), vc.float().clone()
+    kc[:, pos] = k.half().float()
+    vc[:, pos] = v
+    rep = heads // kv_heads
+    keys = kc[:, : pos + 1].repeat_interleave(rep, 0)
+    vals = vc[:, : pos + 1].repeat_interleave(rep, 0)
+    p = torch.softmax((keys @ q.unsqueeze(-1)).squeeze(-1) / 8.0, -1)
+    return (p.unsqueeze(1) @ vals).reshape(-1), k.half()
+
+
+@pytest.mark.parametrize("heads,kv_heads,max_len,pos,splits", [
+    (32, 8, 512, 511, None), (32, 8, 512, 0, None), (32, 8, 512, 200, 1), (32, 8, 128, 63, 128),
+    (8, 8, 256, 100, 3), (4, 1, 96, 95, 5), (32, 1, 64, 40, 2), (32, 8, 4096, 3000, None)])
+def test_decode_attention_matches_fp32_reference(heads, kv_heads, max_len, pos, splits):
+    torch.manual_seed(heads + max_len + pos)
+    qkv = torch.randn((heads + 2 * kv_heads) * 64, device="cuda").half()
+    kc = torch.randn(kv_heads, max_len, 64, device="cuda").half()
+    vc = torch.randn(kv_heads, max_len, 64, device="cuda").half()
+    kc0, vc0 = kc.clone(), vc.clone()
+    cos, sin = _rope_tables(max_len)
+    p = torch.tensor([pos], device="cuda")
+    ref, k_new = _attention_ref(qkv, cos, sin, pos, kc0, vc0, heads, kv_heads)
+    out = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads, splits=splits)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float16 and out.shape == (heads * 64,)
+    err = (out.float() - ref).abs().max().item()
+    assert err <= 2e-3 + 1e-2 * ref.abs().max().item(), err
+    # the cache changed at pos only: v exactly, k up to one fp16 ulp (rounding of the rotation)
+    v_new = qkv[(heads + kv_heads) * 64:].view(kv_heads, 64)
+    assert torch.equal(vc[:, pos], v_new)
+    assert ((kc[:, pos].float() - k_new.float()).abs() <= 1e-3 * k_new.float().abs() + 1e-7).all()
+    keep = torch.ones(max_len, dtype=torch.bool, device="cuda")
+    keep[pos] = False
+    assert torch.equal(kc[:, keep], kc0[:, keep]) and torch.equal(vc[:, keep], vc0[:, keep])
+
+
+def test_decode_attention_repeatable_and_scratch_left_zeroed():
+    heads, kv_heads, max_len = 32, 8, 512
+    qkv = torch.randn((heads + 2 * kv_heads) * 64, device="cuda").half()
+    kc = torch.randn(kv_heads, max_len, 64, device="cuda").half()
+    vc = torch.randn_like(kc)
+    cos, sin = _rope_tables(max_len)
+    p = torch.tensor([300], device="cuda")
+    a = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads).clone()
+    b = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads).clone()
+    assert torch.equal(a, b)
+    scratch = K.kernels._ATTN_SCRATCH[(0, heads, kv_heads, 16)]
+    assert int(scratch[-kv_heads * 4:].count_nonzero()) == 0   # per-kv-head counters back at zero
+
+
+def test_decode_attention_position_out_of_range():
+    heads, kv_heads, max_len = 8, 2, 64
+    qkv = torch.randn((heads + 2 * kv_heads) * 64, device="cuda").half()
+    kc = torch.randn(kv_heads, max_len, 64, device="cuda").half()
+    vc = torch.randn_like(kc)
+    kc0, vc0 = kc.clone(), vc.clone()
+    cos, sin = _rope_tables(max_len)
+    for bad in (max_len, -1):
+        out = K.decode_attention(qkv, cos, sin, torch.tensor([bad], device="cuda"), kc, vc,
+                                 heads=heads, kv_heads=kv_heads, splits=4)
+        torch.cuda.synchronize()
+        assert torch.isnan(out).all()
+        assert torch.equal(kc, kc0) and torch.equal(vc, vc0)
+    good = K.decode_attention(qkv, cos, sin, torch.tensor([10], device="cuda"), kc, vc,
+                              heads=heads, kv_heads=kv_heads, splits=4)
+    assert torch.isfinite(good).all()

@@ -166,6 +166,98 @@ int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_
                      out_dtype, bias, workspace, workspace_bytes, stream);
 }
 
+int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, int group,
+                     int prologue, const void* src, const float* gamma, float eps, int rows,
+                     int cols, void* out, int out_dtype, const float* bias, void* workspace,
+                     size_t workspace_bytes, w4a16_stream_t stream) {
+  if (prologue != W4A16_PROLOGUE_RMSNORM && prologue != W4A16_PROLOGUE_SWIGLU) {
+    set_error("unknown prologue code %d", prologue);
+    return W4A16_ERR_DTYPE;
+  }
+  // src stands in for x in the shared checks (16-byte alignment, non-NULL)
+  int rc = check_gemv(packed, W4A16_PACK_INTERLEAVED, scale, scale_dtype, group, src, 1, rows, cols,
+                      out, out_dtype);
+  if (rc != W4A16_OK || rows == 0) return rc;
+  if (cols % 256 != 0 || !aligned(packed, 16)) {
+    set_error("fused prologue needs cols %% 256 == 0 (got %d) and 16-byte aligned weights", cols);
+    return cols % 256 != 0 ? W4A16_ERR_SHAPE : W4A16_ERR_ALIGN;
+  }
+  if (prologue == W4A16_PROLOGUE_RMSNORM && (!gamma || !aligned(gamma, 16))) {
+    set_error("rmsnorm prologue needs a 16-byte aligned gamma");
+    return gamma ? W4A16_ERR_ALIGN : W4A16_ERR_NULL;
+  }
+  if (bias && !aligned(bias, 4)) {
+    set_error("bias must be 4-byte aligned");
+    return W4A16_ERR_ALIGN;
+  }
+  {  // every CTA reads all of src while rows of out are written
+    const uintptr_t s0 = reinterpret_cast<uintptr_t>(src);
+    const uintptr_t s1 = s0 + (size_t)cols * 4;  // fp32 [cols] or fp16 [2 * cols]
+    const uintptr_t o0 = reinterpret_cast<uintptr_t>(out);
+    const uintptr_t o1 = o0 + (size_t)rows * (out_dtype == W4A16_DTYPE_F32 ? 4 : 2);
+    if (s0 < o1 && o0 < s1) {
+      set_error("out overlaps the prologue source");
+      return W4A16_ERR_SHAPE;
+    }
+  }
+  w4a16::GemvProblem p;
+  p.packed = packed;
+  p.packing = W4A16_PACK_INTERLEAVED;
+  p.scale = scale;
+  p.scale_dtype = scale_dtype;
+  p.group = group;
+  p.x = src;
+  p.M = 1;
+  p.N = rows;
+  p.K = cols;
+  p.y = out;
+  p.out_dtype = out_dtype;
+  p.bias = bias;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace ? workspace_bytes : 0;
+  p.prologue = prologue;
+  p.pro_src = src;
+  p.pro_gamma = gamma;
+  p.pro_eps = eps;
+  p.stream = reinterpret_cast<cudaStream_t>(stream);
+  return w4a16::launch_gemv(p);
+}
+
+int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
+                           const int64_t* pos, void* k_cache, void* v_cache, void* out,
+                           void* scratch, size_t scratch_bytes, int heads, int kv_heads,
+                           int head_dim, int max_len, int splits, w4a16_stream_t stream) {
+  if (!qkv || !cos_t || !sin_t || !pos || !k_cache || !v_cache || !out || !scratch) {
+    set_error("null pointer argument");
+    return W4A16_ERR_NULL;
+  }
+  if (head_dim != 64 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 ||
+      heads / kv_heads > 32 || max_len <= 0 || splits <= 0 || splits > max_len) {
+    set_error("unsupported attention shape: heads %d kv_heads %d head_dim %d max_len %d splits %d "
+              "(head_dim 64, heads %% kv_heads == 0, heads / kv_heads <= 32, 1 <= splits <= max_len)",
+              heads, kv_heads, head_dim, max_len, splits);
+    return W4A16_ERR_SHAPE;
+  }
+  if (!aligned(qkv, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(out, 16) ||
+      !aligned(cos_t, 4) || !aligned(sin_t, 4) || !aligned(pos, 8) || !aligned(scratch, 4)) {
+    set_error("qkv, caches and out must be 16-byte aligned; tables and scratch 4; pos 8");
+    return W4A16_ERR_ALIGN;
+  }
+  if (scratch_bytes < w4a16::decode_attention_scratch_bytes(heads, kv_heads, splits)) {
+    set_error("scratch of %zu bytes is smaller than the %zu needed", scratch_bytes,
+              w4a16::decode_attention_scratch_bytes(heads, kv_heads, splits));
+    return W4A16_ERR_WORKSPACE;
+  }
+  return w4a16::launch_decode_attention(qkv, cos_t, sin_t, reinterpret_cast<const long long*>(pos),
+                                        k_cache, v_cache, out, scratch, heads, kv_heads, head_dim,
+                                        max_len, splits, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t w4a16_decode_attention_scratch_bytes(int heads, int kv_heads, int splits) {
+  if (heads <= 0 || kv_heads <= 0 || splits <= 0) return 0;
+  return w4a16::decode_attention_scratch_bytes(heads, kv_heads, splits);
+}
+
 size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols) {
   return w4a16::gemv_workspace_bytes(batch, rows, cols);
 }

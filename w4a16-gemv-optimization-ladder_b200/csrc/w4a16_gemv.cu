@@ -89,7 +89,17 @@ struct TmaParams {
   int ntiles, kslabs, nwin;
   int nwarps;              // warps that receive work
   int sched;               // kSchedStreamK, kSchedStatic or kSchedDynamic
+  const void* pro_src;     // prologue source (XM 2: fp32 h [K]; XM 3: fp16 gate|up [2K])
+  const float* pro_gamma;  // XM 2: fp32 gamma [K]
+  float pro_eps;           // XM 2: epsilon
 };
+
+// How the single activation vector reaches shared memory (template parameter XM):
+//   kXGlobal   B fragments are loaded from global memory (no staging)
+//   kXCopy     x (fp16 [K]) is copied as is
+//   kXRmsNorm  x = fp16(h * rsqrt(mean(h^2) + eps) * gamma) from an fp32 vector h
+//   kXSwiGlu   x = fp16(silu(g) * u) from an fp16 vector [g (K) | u (K)]
+enum XMode : int { kXGlobal = 0, kXCopy = 1, kXRmsNorm = 2, kXSwiGlu = 3 };
 
 // Work distribution over (16-row tile, 1024-column window) units:
 //   kSchedStreamK  every warp takes an equal contiguous range of units; tiles shared
@@ -272,7 +282,7 @@ __device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
 }
 
 template <int PACK, int GS, typename ST, int NB, typename OT, int WARPS, int STAGES, int SLABS, int RT,
-          bool XS>
+          int XM>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     k_gemv_tma(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const TmaParams p) {
@@ -288,14 +298,65 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int g = lane >> 2;  // MMA group id: rows g and g+8 of each 16-row block
   const int t = lane & 3;   // thread in group: 32-column chunk t of each 128-column group
 
-  // XS: the CTA first copies the activation vector into shared memory (fragment
-  // order, see xs_offset); every B fragment is then one shared-memory load.
+  // XS: the CTA first writes the activation vector into shared memory (fragment
+  // order, see xs_offset), copying it or computing it from the prologue source;
+  // every B fragment is then one shared-memory load.
+  constexpr bool XS = XM != kXGlobal;
   using Plan = SmemPlan<WARPS, STAGES, L>;
   const uint32_t xs = base + (uint32_t)Plan::kXOff;
   if (XS) {
     uint8_t* xsp = smem_raw + (xs - smem_addr(smem_raw));
-    for (int c = threadIdx.x; c < (p.K >> 3); c += blockDim.x)
-      *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = ldg128(p.x + c * 8);
+    const int nch = p.K >> 3;
+    if (XM == kXCopy) {
+      for (int c = threadIdx.x; c < nch; c += blockDim.x)
+        *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = ldg128(p.x + c * 8);
+    } else if (XM == kXRmsNorm) {
+      const float* h = static_cast<const float*>(p.pro_src);
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < p.K; i += blockDim.x) {
+        const float v = __ldg(h + i);
+        ss = fmaf(v, v, ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      float* red = reinterpret_cast<float*>(xsp + (size_t)p.K * 2);  // WARPS partial sums
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      float tot = 0.f;
+      for (int w = 0; w < WARPS; ++w) tot += red[w];
+      const float r = rsqrtf(tot / (float)p.K + p.pro_eps);
+      for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int k = c * 8 + 2 * i;
+          const float a = __ldg(h + k) * r * __ldg(p.pro_gamma + k);
+          const float b = __ldg(h + k + 1) * r * __ldg(p.pro_gamma + k + 1);
+          pk[i] = (uint32_t)__half_as_ushort(__float2half_rn(a)) |
+                  ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+        }
+        *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    } else if (XM == kXSwiGlu) {
+      const __half* gu = static_cast<const __half*>(p.pro_src);
+      for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+        const uint4 gv = ldg128(gu + c * 8);
+        const uint4 uv = ldg128(gu + p.K + c * 8);
+        const uint32_t gw4[4] = {gv.x, gv.y, gv.z, gv.w};
+        const uint32_t uw4[4] = {uv.x, uv.y, uv.z, uv.w};
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gw4[i]));
+          const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uw4[i]));
+          const float a = g2.x / (1.0f + expf(-g2.x)) * u2.x;
+          const float b = g2.y / (1.0f + expf(-g2.y)) * u2.y;
+          pk[i] = (uint32_t)__half_as_ushort(__float2half_rn(a)) |
+                  ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+        }
+        *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
     __syncthreads();
   }
 
@@ -683,11 +744,11 @@ constexpr int tma_smem_bytes() {
   return SmemPlan<kWarps, kStages, L>::kBytes;
 }
 
-template <int PACK, int GS, typename ST, int NB, typename OT, bool XS>
+template <int PACK, int GS, typename ST, int NB, typename OT, int XM>
 int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
   using L = StageLayout<kSlabs, kRT, GS, ST>;
-  auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XS>;
-  const int smem = tma_smem_bytes<GS, ST>() + (XS ? p.K * 2 : 0);
+  auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM>;
+  const int smem = tma_smem_bytes<GS, ST>() + (XM != kXGlobal ? p.K * 2 + 128 : 0);
   if (smem > di.smem_optin) {
     set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
     return W4A16_ERR_SHAPE;
@@ -768,6 +829,9 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   else
     prm.sched = kSchedStreamK;
   prm.nwarps = (int)(prm.sched == kSchedStreamK ? tk : tt);
+  prm.pro_src = p.pro_src;
+  prm.pro_gamma = p.pro_gamma;
+  prm.pro_eps = p.pro_eps;
   prm.partial = nullptr;
   prm.counters = nullptr;
   if (have_ws) {
@@ -801,6 +865,11 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
       (PACK == W4A16_PACK_INTERLEAVED ||
        (GS == 0 && std::is_same<ST, float>::value && std::is_same<OT, float>::value)) &&
       StageLayout<kSlabs, kRT, GS, ST>::kScaleBoxOk;
+  if (p.prologue != W4A16_PROLOGUE_NONE && (!kTmaVariant || !use_tma)) {
+    set_error("fused prologue needs the TMA path: cols %% 256 == 0, 16-byte aligned weights, "
+              "interleaved packing");
+    return W4A16_ERR_SHAPE;
+  }
   if constexpr (!kTmaVariant) {
     (void)use_tma;
     (void)di;
@@ -808,14 +877,27 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
     return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
   } else {
   if (!use_tma) return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
+  const bool xs_fits = tma_smem_bytes<GS, ST>() + p.K * 2 + 128 <= di.smem_optin;
+  if (p.prologue != W4A16_PROLOGUE_NONE) {
+    if (M != 1 || !xs_fits) {
+      set_error("fused prologue needs one activation vector and cols <= %d", (di.smem_optin - tma_smem_bytes<GS, ST>() - 128) / 2);
+      return W4A16_ERR_SHAPE;
+    }
+    if constexpr (PACK == W4A16_PACK_INTERLEAVED) {
+      if (p.prologue == W4A16_PROLOGUE_RMSNORM)
+        return launch_tma<PACK, GS, ST, 1, OT, kXRmsNorm>(p, x, M, y, di, dev);
+      return launch_tma<PACK, GS, ST, 1, OT, kXSwiGlu>(p, x, M, y, di, dev);
+    }
+    set_error("fused prologues take the interleaved packing");
+    return W4A16_ERR_DTYPE;
+  }
   if (M == 1) {
     // one activation vector: keep it in shared memory when it fits beside the ring
-    if (tma_smem_bytes<GS, ST>() + p.K * 2 <= di.smem_optin)
-      return launch_tma<PACK, GS, ST, 1, OT, true>(p, x, M, y, di, dev);
-    return launch_tma<PACK, GS, ST, 1, OT, false>(p, x, M, y, di, dev);
+    if (xs_fits) return launch_tma<PACK, GS, ST, 1, OT, kXCopy>(p, x, M, y, di, dev);
+    return launch_tma<PACK, GS, ST, 1, OT, kXGlobal>(p, x, M, y, di, dev);
   }
-  if (M <= 8) return launch_tma<PACK, GS, ST, 8, OT, false>(p, x, M, y, di, dev);
-  return launch_tma<PACK, GS, ST, 16, OT, false>(p, x, M, y, di, dev);
+  if (M <= 8) return launch_tma<PACK, GS, ST, 8, OT, kXGlobal>(p, x, M, y, di, dev);
+  return launch_tma<PACK, GS, ST, 16, OT, kXGlobal>(p, x, M, y, di, dev);
   }
 }
 

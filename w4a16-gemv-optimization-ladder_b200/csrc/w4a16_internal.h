@@ -25,7 +25,11 @@ struct GemvProblem {
   const float* bias = nullptr;      // fp32 [N] or null
   void* workspace = nullptr;        // split-K partials + tile counters (zero-filled once)
   size_t workspace_bytes = 0;
-  int split_k = 0;                  // 0 = choose, 1 = off, >1 = requested split count
+  int split_k = 0;                  // 0 = choose, 1 = no workspace schedules
+  int prologue = W4A16_PROLOGUE_NONE;  // x computed from pro_src inside the kernel
+  const void* pro_src = nullptr;
+  const float* pro_gamma = nullptr;
+  float pro_eps = 0.f;
   cudaStream_t stream = nullptr;
 };
 
@@ -56,6 +60,14 @@ int launch_dequant(const uint8_t* packed, int packing, const void* scale, int sc
 //   scale = absmax / 7 per row or group, q = clamp(rint(w / scale), -8, 7).
 int launch_quantize_pack(const void* w, int w_dtype, int rows, int cols, int group, int packing,
                          uint8_t* packed, void* scale, int scale_dtype, cudaStream_t stream);
+
+// Decode-step attention (one token, head_dim 64) fused with rotary and the KV-cache
+// write; scratch holds per-split partials and per-kv-head counters (zero-filled once).
+size_t decode_attention_scratch_bytes(int heads, int kv_heads, int splits);
+int launch_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
+                            const long long* pos, void* k_cache, void* v_cache, void* out,
+                            void* scratch, int heads, int kv_heads, int head_dim, int max_len,
+                            int splits, cudaStream_t stream);
 
 // Reads (and clears) the device-side error word written by kernels whose bounded
 // waits ran out.  Synchronises `stream`.

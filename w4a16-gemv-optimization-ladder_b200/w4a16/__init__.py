@@ -5,8 +5,11 @@ Drop-in for the Python surface of the reference package `w4a16`
 hand-written sm_100a kernels behind the C ABI of libw4a16_b200.so.
 """
 from .kernels import (
+    decode_attention,
     dequant_int4,
     gemv,
+    gemv_rmsnorm,
+    gemv_swiglu,
     matvec_byte,
     matvec_champ,
     matvec_fp16,
@@ -38,6 +41,6 @@ __all__ = [
     "quantize_int4_symmetric", "quantize_int4_group", "pack_int4", "pack_int4_interleaved",
     "dequant_ref", "dequant_ref_group", "W4A16Linear", "replace_linear_with_w4a16",
     # additions
-    "gemv", "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace",
+    "gemv", "gemv_rmsnorm", "gemv_swiglu", "decode_attention", "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace",
     "read_device_error",
 ]

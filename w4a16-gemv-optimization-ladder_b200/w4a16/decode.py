@@ -1,0 +1,272 @@
+"""One-token decode step of a Llama-architecture model on the W4A16 kernels.
+
+The reference measures end-to-end decode by swapping the Linears of a Hugging Face
+Llama-3.2-1B and looping `model(next_token, past_key_values=...)` from Python
+(benchmarks/end_to_end.py:24-42): every token drives ~113 GEMVs plus the model's
+other kernels from the host.  Here the same architecture (random weights; there is no
+checkpoint offline) runs as a fixed sequence of device operations over a static KV
+cache, captured once in a CUDA graph and replayed per token.  With `fused=True` (the
+default for int4 weights) a layer is five launches:
+
+  qkv = W_qkv fp16(rmsnorm(h))           gemv_rmsnorm  (norm in the GEMV prologue)
+  attn = attention(rotary(q, k), cache)  decode_attention (also writes k, v at pos)
+  h += W_o attn                          gemv          (residual in the epilogue)
+  gu = W_gu fp16(rmsnorm(h))             gemv_rmsnorm
+  h += W_down fp16(silu(g) * u)          gemv_swiglu   (activation in the prologue)
+
+and the head is logits = W_lm fp16(rmsnorm(h)) (gemv_rmsnorm).  All projections are
+int4 with group-128 scales; the residual stream h is fp32.  `fused=False` runs the
+same GEMVs with the norms, rotary, cache write, attention (SDPA) and SwiGLU as torch
+ops in between; `dense=True` builds the model with fp16 weights on cuBLAS (`F.linear`)
+and the torch ops, for comparison.
+"""
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+
+GROUP = 128
+
+
+@dataclass
+class LlamaDecodeConfig:
+    hidden: int = 2048
+    intermediate: int = 8192
+    layers: int = 16
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 64
+    vocab: int = 128256
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+    max_len: int = 512          # KV cache length
+
+    @property
+    def qkv_rows(self):
+        return (self.heads + 2 * self.kv_heads) * self.head_dim
+
+
+LLAMA_3_2_1B = LlamaDecodeConfig()
+
+
+class _Proj:
+    """One projection: int4 packed + group-128 scales, or a dense fp16 weight."""
+
+    def __init__(self, w, dense):
+        self.rows, self.cols = w.shape
+        self.dense = dense
+        if dense:
+            self.w = w.half().contiguous()
+        else:
+            self.packed, self.scale = K.quantize_pack(w.contiguous(), group=GROUP)
+
+    def bytes(self):
+        if self.dense:
+            return self.w.numel() * 2
+        return self.packed.numel() + self.scale.numel() * self.scale.element_size()
+
+    def dequantized(self):
+        if self.dense:
+            return self.w.float()
+        return K.dequant_int4(self.packed, self.scale, group=GROUP).float()
+
+    def __call__(self, x, out=None, residual=None, out_dtype=torch.float16):
+        """out = W x (+ residual); x fp16 [cols].  residual (fp32 [rows]) may alias out."""
+        if self.dense:
+            y = F.linear(x.view(1, -1), self.w).view(-1)
+            if residual is not None:
+                out.copy_(residual + y.float())
+                return out
+            return y if out is None else out.copy_(y)
+        if out is None:
+            out = torch.empty(self.rows, dtype=out_dtype, device=x.device)
+        return K.gemv(self.packed, self.scale, x, group=GROUP, bias=residual, out=out,
+                      out_dtype=out.dtype)
+
+
+class W4A16LlamaDecoder:
+    """Random-init Llama decoder for one-token steps (batch 1) over a static KV cache."""
+
+    def __init__(self, cfg=LLAMA_3_2_1B, device="cuda", seed=0, dense=False, std=0.02, fused=None):
+        self.cfg = cfg
+        self.dense = dense
+        self.fused = (not dense) if fused is None else bool(fused)
+        if self.fused and (dense or cfg.head_dim != 64):
+            raise ValueError("the fused step needs int4 weights and head_dim 64")
+        dev = torch.device(device)
+        self.device = dev
+        g = torch.Generator(device=dev).manual_seed(seed)
+        H, I, D = cfg.hidden, cfg.intermediate, cfg.head_dim
+
+        def rnd(*shape):
+            return (torch.randn(*shape, device=dev, generator=g) * std).half()
+
+        self.embed = rnd(cfg.vocab, H)
+        self.layers = []
+        for _ in range(cfg.layers):
+            self.layers.append(dict(
+                qkv=_Proj(rnd(cfg.qkv_rows, H), dense),
+                o=_Proj(rnd(H, cfg.heads * D), dense),
+                gu=_Proj(rnd(2 * I, H), dense),
+                down=_Proj(rnd(H, I), dense),
+                norm_attn=torch.ones(H, device=dev),
+                norm_mlp=torch.ones(H, device=dev),
+            ))
+        self.norm_final = torch.ones(H, device=dev)
+        self.lm_head = _Proj(self.embed, dense)  # tied to the embedding, as in Llama-3.2-1B
+        # rotary tables (Llama's rotate-half convention)
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=dev).float() / D))
+        ang = torch.arange(cfg.max_len, device=dev).float()[:, None] * inv[None, :]
+        self.cos = torch.cat([ang.cos(), ang.cos()], dim=1)   # [L, D]
+        self.sin = torch.cat([ang.sin(), ang.sin()], dim=1)
+        # static state
+        self.k_cache = torch.zeros(cfg.layers, cfg.kv_heads, cfg.max_len, D, dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.token = torch.zeros(1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self.h = torch.empty(H, dtype=torch.float32, device=dev)
+        self.qkv = torch.empty(cfg.qkv_rows, dtype=torch.float16, device=dev)
+        self.gu = torch.empty(2 * I, dtype=torch.float16, device=dev)
+        self.attn = torch.empty(cfg.heads * D, dtype=torch.float16, device=dev)
+        self.logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
+        self.graph = None
+
+    # ------------------------------------------------------------------ pieces
+
+    def weight_bytes(self):
+        per = sum(p.bytes() for L in self.layers for p in (L["qkv"], L["o"], L["gu"], L["down"]))
+        return per + self.lm_head.bytes()
+
+    def fill_cache(self, length, seed=1):
+        """Random keys/values for positions [0, length) (a stand-in for a prompt)."""
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        self.k_cache[:, :, :length].normal_(generator=g)
+        self.v_cache[:, :, :length].normal_(generator=g)
+
+    def _rmsnorm(self, h, w):
+        return (h * torch.rsqrt(h.pow(2).mean() + self.cfg.eps) * w).half()
+
+    def _rope(self, x, heads):
+        D = self.cfg.head_dim
+        x = x.view(heads, D).float()
+        cos = self.cos.index_select(0, self.pos)    # [1, D]
+        sin = self.sin.index_select(0, self.pos)
+        rot = torch.cat([-x[:, D // 2:], x[:, :D // 2]], dim=1)
+        return (x * cos + rot * sin).half()
+
+    def _attention(self, q, li):
+        cfg = self.cfg
+        L = cfg.max_len
+        kc = self.k_cache[li].view(1, cfg.kv_heads, L, cfg.head_dim)
+        vc = self.v_cache[li].view(1, cfg.kv_heads, L, cfg.head_dim)
+        mask = torch.where(torch.arange(L, device=self.device) <= self.pos, 0.0, float("-inf"))
+        out = F.scaled_dot_product_attention(q.view(1, cfg.heads, 1, cfg.head_dim), kc, vc,
+                                             attn_mask=mask.view(1, 1, 1, L).half(), enable_gqa=True)
+        return out.reshape(-1)
+
+    def _step_fused(self):
+        cfg = self.cfg
+        G = GROUP
+        self.h.copy_(self.embed.index_select(0, self.token).view(-1))
+        for li, L in enumerate(self.layers):
+            qkv, o, gu, down = L["qkv"], L["o"], L["gu"], L["down"]
+            K.gemv_rmsnorm(qkv.packed, qkv.scale, self.h, L["norm_attn"], cfg.eps, group=G, out=self.qkv)
+            K.decode_attention(self.qkv, self.cos, self.sin, self.pos, self.k_cache[li], self.v_cache[li],
+                               heads=cfg.heads, kv_heads=cfg.kv_heads, out=self.attn)
+            K.gemv(o.packed, o.scale, self.attn, group=G, bias=self.h, out=self.h)
+            K.gemv_rmsnorm(gu.packed, gu.scale, self.h, L["norm_mlp"], cfg.eps, group=G, out=self.gu)
+            K.gemv_swiglu(down.packed, down.scale, self.gu, group=G, bias=self.h, out=self.h)
+        head = self.lm_head
+        K.gemv_rmsnorm(head.packed, head.scale, self.h, self.norm_final, cfg.eps, group=G, out=self.logits)
+        return self.logits
+
+    def _step(self):
+        if self.fused:
+            return self._step_fused()
+        cfg = self.cfg
+        nq, nk = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        self.h.copy_(self.embed.index_select(0, self.token).view(-1).float())
+        for li, L in enumerate(self.layers):
+            x = self._rmsnorm(self.h, L["norm_attn"])
+            L["qkv"](x, out=self.qkv)
+            q = self._rope(self.qkv[:nq], cfg.heads)
+            k = self._rope(self.qkv[nq:nq + nk], cfg.kv_heads)
+            v = self.qkv[nq + nk:].view(cfg.kv_heads, cfg.head_dim)
+            self.k_cache[li].index_copy_(1, self.pos, k.view(cfg.kv_heads, 1, cfg.head_dim))
+            self.v_cache[li].index_copy_(1, self.pos, v.view(cfg.kv_heads, 1, cfg.head_dim))
+            attn = self._attention(q, li)
+            L["o"](attn, out=self.h, residual=self.h)
+            x = self._rmsnorm(self.h, L["norm_mlp"])
+            L["gu"](x, out=self.gu)
+            a = (F.silu(self.gu[:cfg.intermediate].float()) * self.gu[cfg.intermediate:].float()).half()
+            L["down"](a, out=self.h, residual=self.h)
+        x = self._rmsnorm(self.h, self.norm_final)
+        self.lm_head(x, out=self.logits)
+        return self.logits
+
+    # ------------------------------------------------------------------- public
+
+    def step(self, token, pos):
+        """Eager step: logits (fp32 [vocab]) for `token` at position `pos`."""
+        self.token.fill_(int(token))
+        self.pos.fill_(int(pos))
+        return self._step()
+
+    def capture(self):
+        """Record one decode step in a CUDA graph (token and pos are read on the device)."""
+        K.reserve_workspace(self.device, 1, self.cfg.vocab, self.cfg.hidden)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside capture
+                self._step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._step()
+        return self.graph
+
+    def replay(self, token, pos):
+        """Graph step: set token/pos on the device, replay, return the logits buffer."""
+        self.token.fill_(int(token))
+        self.pos.fill_(int(pos))
+        self.graph.replay()
+        return self.logits
+
+    def reference_logits(self, token, pos):
+        """The same step in fp32 torch from the dequantised weights (test reference).
+
+        Uses and updates a copy of the caches, so the decoder's own state is unchanged."""
+        cfg = self.cfg
+        D, nq, nk = cfg.head_dim, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+        kc, vc = self.k_cache.float().clone(), self.v_cache.float().clone()
+        p = int(pos)
+        h = self.embed[int(token)].float()
+
+        def norm(v, w):
+            return v * torch.rsqrt(v.pow(2).mean() + cfg.eps) * w
+
+        def rope(v, heads):
+            v = v.view(heads, D)
+            rot = torch.cat([-v[:, D // 2:], v[:, :D // 2]], dim=1)
+            return v * self.cos[p] + rot * self.sin[p]
+
+        for li, L in enumerate(self.layers):
+            x = norm(h, L["norm_attn"]).half().float()
+            qkv = L["qkv"].dequantized() @ x
+            q, k = rope(qkv[:nq], cfg.heads), rope(qkv[nq:nq + nk], cfg.kv_heads)
+            kc[li, :, p] = k
+            vc[li, :, p] = qkv[nq + nk:].view(cfg.kv_heads, D)
+            rep = cfg.heads // cfg.kv_heads
+            keys = kc[li, :, : p + 1].repeat_interleave(rep, 0)      # [heads, p+1, D]
+            vals = vc[li, :, : p + 1].repeat_interleave(rep, 0)
+            att = torch.softmax((keys @ q.unsqueeze(-1)).squeeze(-1) / D ** 0.5, dim=-1)
+            attn = (att.unsqueeze(1) @ vals).reshape(-1)
+            h = h + L["o"].dequantized() @ attn
+            x = norm(h, L["norm_mlp"]).half().float()
+            gu = L["gu"].dequantized() @ x
+            a = F.silu(gu[:cfg.intermediate]) * gu[cfg.intermediate:]
+            h = h + L["down"].dequantized() @ a
+        return self.lm_head.dequantized() @ norm(h, self.norm_final)

@@ -135,6 +135,101 @@ def gemv(packed, scale, x, *, group=0, packing="interleaved", bias=None, out_dty
     return out
 
 
+def _fused(prologue, packed, scale, src, gamma, eps, group, bias, out, out_dtype, split_k):
+    _check_packed(packed)
+    rows, cols = packed.shape[0], packed.shape[1] * 2
+    dev = packed.device
+    _need(group in (0, GROUP), f"group must be 0 or {GROUP}")
+    _need(isinstance(scale, torch.Tensor) and scale.device == dev and scale.dtype in _SCALE_DTYPES
+          and scale.is_contiguous(), "scale must be a contiguous float32/float16 CUDA tensor")
+    if out is None:
+        out = torch.empty(rows, dtype=out_dtype, device=dev)
+    _need(out.device == dev and out.dtype in _OUT_DTYPES and tuple(out.shape) == (rows,)
+          and out.is_contiguous(), "out must be a contiguous fp32/fp16 [rows] tensor")
+    if bias is not None:
+        _need(bias.device == dev and bias.dtype == torch.float32 and tuple(bias.shape) == (rows,)
+              and bias.is_contiguous(), "bias must be a contiguous float32 [rows] tensor")
+    ws = _workspace(dev, 1, rows, cols) if split_k else None
+    with torch.cuda.device(dev):
+        status = _lib.lib().w4a16_gemv_fused(
+            _ptr(packed), _ptr(scale), _SCALE_DTYPES[scale.dtype], group, prologue, _ptr(src),
+            _ptr(gamma), float(eps), rows, cols, _ptr(out), _OUT_DTYPES[out.dtype], _ptr(bias),
+            _ptr(ws), ws.numel() if ws is not None else 0, _stream(dev))
+    _lib.check(status, "w4a16_gemv_fused")
+    return out
+
+
+def gemv_rmsnorm(packed, scale, h, gamma, eps=1e-5, *, group=0, bias=None, out=None,
+                 out_dtype=torch.float32, split_k=True):
+    """W @ fp16(h * rsqrt(mean(h^2) + eps) * gamma) (+ bias): RMSNorm fused into the GEMV.
+
+    h, gamma: fp32 [cols] on the weights' device.  out may alias bias (in-place residual)."""
+    cols = packed.shape[1] * 2
+    for name, t in (("h", h), ("gamma", gamma)):
+        _need(isinstance(t, torch.Tensor) and t.device == packed.device and t.dtype == torch.float32
+              and tuple(t.shape) == (cols,) and t.is_contiguous(), f"{name} must be fp32 [{cols}]")
+    return _fused(_lib.PROLOGUE_RMSNORM, packed, scale, h, gamma, eps, group, bias, out, out_dtype,
+                  split_k)
+
+
+def gemv_swiglu(packed, scale, gate_up, *, group=0, bias=None, out=None, out_dtype=torch.float32,
+                split_k=True):
+    """W @ fp16(silu(gate) * up) (+ bias) with gate_up = [gate | up] fp16 [2 * cols]."""
+    cols = packed.shape[1] * 2
+    _need(isinstance(gate_up, torch.Tensor) and gate_up.device == packed.device
+          and gate_up.dtype == torch.float16 and tuple(gate_up.shape) == (2 * cols,)
+          and gate_up.is_contiguous(), f"gate_up must be fp16 [{2 * cols}]")
+    return _fused(_lib.PROLOGUE_SWIGLU, packed, scale, gate_up, None, 0.0, group, bias, out, out_dtype,
+                  split_k)
+
+
+_ATTN_SCRATCH = {}
+
+
+def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, out=None, splits=None):
+    """One decode token's attention with rotary and the KV-cache write in one launch.
+
+    qkv fp16 [(heads + 2 kv_heads) * 64] (q | k | v); cos, sin fp32 [max_len, 64]
+    (rotate-half tables); pos int64 [1] on the device; k_cache, v_cache fp16
+    [kv_heads, max_len, 64] (this layer's).  Writes k_cache/v_cache at pos and returns
+    out fp16 [heads * 64].  splits: CTAs per kv head over the positions (default one per
+    32 positions).  The zeroed scratch is kept per device and shape; allocate it (one
+    eager call) before capturing the op in a CUDA graph."""
+    dev = qkv.device
+    D = 64
+    max_len = k_cache.shape[1]
+    _need(qkv.dtype == torch.float16 and qkv.is_cuda and qkv.is_contiguous()
+          and tuple(qkv.shape) == ((heads + 2 * kv_heads) * D,), "qkv must be fp16 [(heads + 2 kv_heads) * 64]")
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache)):
+        _need(t.device == dev and t.dtype == torch.float16 and t.is_contiguous()
+              and tuple(t.shape) == (kv_heads, max_len, D), f"{name} must be fp16 [kv_heads, max_len, 64]")
+    for name, t in (("cos", cos), ("sin", sin)):
+        _need(t.device == dev and t.dtype == torch.float32 and t.is_contiguous()
+              and t.dim() == 2 and t.shape[1] == D and t.shape[0] >= max_len, f"{name} must be fp32 [>= max_len, 64]")
+    _need(pos.device == dev and pos.dtype == torch.int64 and pos.numel() == 1, "pos must be int64 [1] on the device")
+    if splits is None:
+        splits = max(1, (max_len + 31) // 32)
+    if out is None:
+        out = torch.empty(heads * D, dtype=torch.float16, device=dev)
+    _need(out.device == dev and out.dtype == torch.float16 and tuple(out.shape) == (heads * D,)
+          and out.is_contiguous(), "out must be fp16 [heads * 64]")
+    L = _lib.lib()
+    need = L.w4a16_decode_attention_scratch_bytes(heads, kv_heads, splits)
+    key = (dev.index, heads, kv_heads, splits)
+    scratch = _ATTN_SCRATCH.get(key)
+    if scratch is None:
+        _need(not torch.cuda.is_current_stream_capturing(),
+              "decode_attention scratch must exist before capture: call it once eagerly")
+        scratch = torch.zeros(need, dtype=torch.uint8, device=dev)
+        _ATTN_SCRATCH[key] = scratch
+    with torch.cuda.device(dev):
+        status = L.w4a16_decode_attention(
+            _ptr(qkv), _ptr(cos), _ptr(sin), _ptr(pos), _ptr(k_cache), _ptr(v_cache), _ptr(out),
+            _ptr(scratch), scratch.numel(), heads, kv_heads, D, max_len, splits, _stream(dev))
+    _lib.check(status, "w4a16_decode_attention")
+    return out
+
+
 # ------------------------------------------------------- reference-named ops
 
 def _ref_call(name, packed, scale, vec, group, packing):
