@@ -52,6 +52,14 @@ enum w4a16_dtype { W4A16_DTYPE_F32 = 0, W4A16_DTYPE_F16 = 1 };
 enum w4a16_packing { W4A16_PACK_INTERLEAVED = 0, W4A16_PACK_SIMPLE = 1 };
 enum w4a16_prologue { W4A16_PROLOGUE_NONE = 0, W4A16_PROLOGUE_RMSNORM = 1, W4A16_PROLOGUE_SWIGLU = 2 };
 
+/* Launch flags of the decode-step entries (w4a16_gemv_fused, w4a16_decode_attention).
+ * W4A16_LAUNCH_PDL: programmatic dependent launch.  The kernel may start while the
+ * previous kernel in the stream is still running: it loads its weights, then waits for
+ * that kernel to finish before reading anything the kernel wrote, and lets the next
+ * kernel start in turn.  Use it between these entries (a normal launch before or after
+ * is unaffected); two consecutive calls must not share a workspace or scratch buffer. */
+enum w4a16_launch_flags { W4A16_LAUNCH_PDL = 1 };
+
 /* ---------------------------------------------------------------------------
  * Reference-mirroring entry points: out[r] = sum_k q[r][k] * scale * vec[k], fp32.
  * ------------------------------------------------------------------------- */
@@ -111,28 +119,32 @@ int w4a16_fp16_cuda(const void* mat, const void* vec, float* out, int rows, int 
  *              least w4a16_gemv_workspace_bytes(batch, rows, cols) it lets every
  *              warp take an equal share of the work (tiles shared by two warps are
  *              reduced through it); without it each warp owns whole 16-row tiles.
- *              The kernels leave it zeroed.  Calls that share a workspace must be
+ *              The kernels leave its counter block zeroed, so zero-filling once is
+ *              enough (the partial sums are scratch).  Calls that share a workspace must be
  *              ordered on one stream. */
 int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_dtype, int group,
                const void* x, int batch, int rows, int cols, void* out, int out_dtype,
                const float* bias, void* workspace, size_t workspace_bytes,
                w4a16_stream_t stream);
 
-/* w4a16_gemv with the activation computed inside the kernel, for decode steps of
- * Llama-style models.  The reference applies these operations as separate torch ops
- * between its GEMVs (the HF model around W4A16Linear, src/w4a16/kernels.py:113-124);
- * here they are the prologue of the GEMV that consumes them:
+/* w4a16_gemv for one activation vector held in shared memory, the GEMV of a decode
+ * step of a Llama-style model, with the activation optionally computed inside the
+ * kernel.  The reference applies these operations as separate torch ops between its
+ * GEMVs (the HF model around W4A16Linear, src/w4a16/kernels.py:113-124); here they are
+ * the prologue of the GEMV that consumes them:
+ *   W4A16_PROLOGUE_NONE     src = fp16 x [cols]
  *   W4A16_PROLOGUE_RMSNORM  src = fp32 h [cols], gamma = fp32 [cols]:
  *                           x = fp16(h * rsqrt(mean(h^2) + eps) * gamma)
  *   W4A16_PROLOGUE_SWIGLU   src = fp16 [2*cols] = gate | up:  x = fp16(silu(gate) * up)
  * One activation vector; interleaved packing; cols % 256 == 0 and small enough for the
  * vector to sit in shared memory beside the weight rings (cols <= 10752 with group-128
- * fp32 scales, <= 16896 with one scale per row).  out (fp32 or fp16 [rows]) may alias bias
- * (fp32): out = W x + bias is then an in-place residual add.  out must not overlap src. */
+ * fp32 scales, <= 16896 with one scale per row).  out (fp32 or fp16 [rows]) may alias
+ * bias (fp32): out = W x + bias is then an in-place residual add.  out must not overlap
+ * src.  flags: 0 or W4A16_LAUNCH_PDL. */
 int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, int group,
                      int prologue, const void* src, const float* gamma, float eps, int rows,
                      int cols, void* out, int out_dtype, const float* bias, void* workspace,
-                     size_t workspace_bytes, w4a16_stream_t stream);
+                     size_t workspace_bytes, unsigned flags, w4a16_stream_t stream);
 
 /* Decode-step attention of a Llama-style layer for one token (batch 1), the kernel
  * that sits between the QKV and output GEMVs of a decode step.  The reference leaves
@@ -146,11 +158,13 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
  * fp32 partial softmaxes are combined by the last one; scratch is a zero-filled device
  * buffer of w4a16_decode_attention_scratch_bytes(heads, kv_heads, splits) bytes that the
  * kernel leaves zeroed.  A position outside [0, max_len) writes nothing to the caches and
- * NaN to out.  Calls sharing a scratch buffer must be ordered on one stream. */
+ * NaN to out.  Calls sharing a scratch buffer must be ordered on one stream.  flags: 0 or
+ * W4A16_LAUNCH_PDL. */
 int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
                            const int64_t* pos, void* k_cache, void* v_cache, void* out,
                            void* scratch, size_t scratch_bytes, int heads, int kv_heads,
-                           int head_dim, int max_len, int splits, w4a16_stream_t stream);
+                           int head_dim, int max_len, int splits, unsigned flags,
+                           w4a16_stream_t stream);
 
 size_t w4a16_decode_attention_scratch_bytes(int heads, int kv_heads, int splits);
 

@@ -104,15 +104,17 @@ def test_python_ops_fail_loudly_without_library(monkeypatch, tmp_path):
         _lib.lib.cache_clear()
 
 
-def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0):
+def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0, flags=0):
     return lib.w4a16_gemv_fused(ctypes.c_void_p(1 << 12), ctypes.c_void_p(1 << 12), 0, 0, prologue,
                                 ctypes.c_void_p(src), ctypes.c_void_p(gamma), 1e-5, rows, cols,
-                                ctypes.c_void_p(out), odt, None, None, 0, None)
+                                ctypes.c_void_p(out), odt, None, None, 0, flags, None)
 
 
 def test_fused_gemv_host_validation(lib):
-    assert _fused(lib, prologue=0) == -4                 # only the RMSNorm / SwiGLU prologues
+    assert _fused(lib, prologue=3) == -4                 # NONE, RMSNorm or SwiGLU only
     assert _fused(lib, prologue=7) == -4
+    assert _fused(lib, flags=2) == -4                    # only W4A16_LAUNCH_PDL
+    assert _fused(lib, prologue=0, out=(1 << 16) + 256) == -2   # x fp16 [256] = 512 bytes
     assert _fused(lib, src=0) == -1
     assert _fused(lib, gamma=0) == -1                    # RMSNorm needs gamma
     assert _fused(lib, gamma=(1 << 20) + 4) == -3
@@ -124,11 +126,11 @@ def test_fused_gemv_host_validation(lib):
 
 
 def _attn(lib, qkv=1 << 12, pos=1 << 13, scratch=1 << 14, scratch_bytes=1 << 20, heads=32,
-          kv_heads=8, head_dim=64, max_len=512, splits=16):
+          kv_heads=8, head_dim=64, max_len=512, splits=16, flags=0):
     p = ctypes.c_void_p
     return lib.w4a16_decode_attention(p(qkv), p(1 << 15), p(1 << 15), p(pos), p(1 << 16), p(1 << 17),
                                       p(1 << 18), p(scratch), scratch_bytes, heads, kv_heads, head_dim,
-                                      max_len, splits, None)
+                                      max_len, splits, flags, None)
 
 
 def test_decode_attention_host_validation(lib):
@@ -145,3 +147,4 @@ def test_decode_attention_host_validation(lib):
     assert _attn(lib, pos=(1 << 13) + 4) == -3
     assert _attn(lib, scratch_bytes=100) == -5
     assert b"scratch" in lib.w4a16_last_error_string()
+    assert _attn(lib, flags=4) == -4

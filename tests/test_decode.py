@@ -63,3 +63,19 @@ def test_full_size_weight_bytes():
     logits = dec.replay(token=1, pos=511)
     torch.cuda.synchronize()
     assert torch.isfinite(logits).all()
+
+
+def test_chained_launches_change_nothing():
+    # the fused step with programmatic dependent launch equals the one without, bit for bit
+    from w4a16.decode import W4A16LlamaDecoder
+
+    outs = []
+    for pdl in (False, True):
+        dec = W4A16LlamaDecoder(_small(), seed=6, pdl=pdl)
+        assert dec.pdl == pdl
+        dec.fill_cache(70)
+        outs.append(dec.step(token=9, pos=70).clone())
+        dec.capture()
+        outs.append(dec.replay(token=9, pos=70).clone())
+    torch.cuda.synchronize()
+    assert all(torch.equal(outs[0], o) for o in outs[1:])

@@ -169,9 +169,14 @@ int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_
 int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, int group,
                      int prologue, const void* src, const float* gamma, float eps, int rows,
                      int cols, void* out, int out_dtype, const float* bias, void* workspace,
-                     size_t workspace_bytes, w4a16_stream_t stream) {
-  if (prologue != W4A16_PROLOGUE_RMSNORM && prologue != W4A16_PROLOGUE_SWIGLU) {
+                     size_t workspace_bytes, unsigned flags, w4a16_stream_t stream) {
+  if (prologue != W4A16_PROLOGUE_NONE && prologue != W4A16_PROLOGUE_RMSNORM &&
+      prologue != W4A16_PROLOGUE_SWIGLU) {
     set_error("unknown prologue code %d", prologue);
+    return W4A16_ERR_DTYPE;
+  }
+  if (flags & ~(unsigned)W4A16_LAUNCH_PDL) {
+    set_error("unknown launch flags 0x%x", flags);
     return W4A16_ERR_DTYPE;
   }
   // src stands in for x in the shared checks (16-byte alignment, non-NULL)
@@ -192,7 +197,7 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
   }
   {  // every CTA reads all of src while rows of out are written
     const uintptr_t s0 = reinterpret_cast<uintptr_t>(src);
-    const uintptr_t s1 = s0 + (size_t)cols * 4;  // fp32 [cols] or fp16 [2 * cols]
+    const uintptr_t s1 = s0 + (size_t)cols * (prologue == W4A16_PROLOGUE_NONE ? 2 : 4);
     const uintptr_t o0 = reinterpret_cast<uintptr_t>(out);
     const uintptr_t o1 = o0 + (size_t)rows * (out_dtype == W4A16_DTYPE_F32 ? 4 : 2);
     if (s0 < o1 && o0 < s1) {
@@ -219,6 +224,8 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
   p.pro_src = src;
   p.pro_gamma = gamma;
   p.pro_eps = eps;
+  p.staged = true;
+  p.pdl = (flags & W4A16_LAUNCH_PDL) != 0;
   p.stream = reinterpret_cast<cudaStream_t>(stream);
   return w4a16::launch_gemv(p);
 }
@@ -226,7 +233,12 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
 int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
                            const int64_t* pos, void* k_cache, void* v_cache, void* out,
                            void* scratch, size_t scratch_bytes, int heads, int kv_heads,
-                           int head_dim, int max_len, int splits, w4a16_stream_t stream) {
+                           int head_dim, int max_len, int splits, unsigned flags,
+                           w4a16_stream_t stream) {
+  if (flags & ~(unsigned)W4A16_LAUNCH_PDL) {
+    set_error("unknown launch flags 0x%x", flags);
+    return W4A16_ERR_DTYPE;
+  }
   if (!qkv || !cos_t || !sin_t || !pos || !k_cache || !v_cache || !out || !scratch) {
     set_error("null pointer argument");
     return W4A16_ERR_NULL;
@@ -250,7 +262,8 @@ int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin
   }
   return w4a16::launch_decode_attention(qkv, cos_t, sin_t, reinterpret_cast<const long long*>(pos),
                                         k_cache, v_cache, out, scratch, heads, kv_heads, head_dim,
-                                        max_len, splits, reinterpret_cast<cudaStream_t>(stream));
+                                        max_len, splits, (flags & W4A16_LAUNCH_PDL) != 0,
+                                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t w4a16_decode_attention_scratch_bytes(int heads, int kv_heads, int splits) {

@@ -47,150 +47,220 @@ __device__ __forceinline__ void rope_pair(float& a, float& b, const float* cos_r
   b = rb;
 }
 
-__global__ void k_decode_attention(const __half* __restrict__ qkv, const float* __restrict__ cos_t,
+template <int MAXT>
+__global__ void __launch_bounds__(MAXT) k_decode_attention(const __half* qkv, const float* __restrict__ cos_t,
                                    const float* __restrict__ sin_t, const long long* __restrict__ pos_p,
-                                   __half* __restrict__ k_cache, __half* __restrict__ v_cache,
-                                   __half* __restrict__ out, float* __restrict__ scratch, int heads,
-                                   int kv_heads, int max_len, int splits, float scale) {
+                                   __half* k_cache, __half* v_cache, __half* __restrict__ out,
+                                   float* __restrict__ scratch, int heads, int kv_heads, int max_len,
+                                   int splits, float scale) {
   const int kvh = blockIdx.x / splits;
   const int split = blockIdx.x % splits;
   const int group = heads / kv_heads;
   const int warp = threadIdx.x >> 5;  // query head within the group
   const int lane = threadIdx.x & 31;
   const int head = kvh * group + warp;
-  const long long pos_ll = pos_p[0];
-  if (pos_ll < 0 || pos_ll >= max_len) {  // nothing is read or written: the heads read NaN
-    if (split == 0) {
-      out[head * kHeadDim + lane] = __float2half_rn(__int_as_float(0x7fc00000));
-      out[head * kHeadDim + lane + 32] = __float2half_rn(__int_as_float(0x7fc00000));
-    }
-    return;
-  }
-  const int pos = (int)pos_ll;
+  const long long pos_ll = pos_p[0];  // set before the step, not by the previous kernel
+  const bool bad_pos = pos_ll < 0 || pos_ll >= max_len;
+  const int pos = bad_pos ? 0 : (int)pos_ll;
   const int span = (max_len + splits - 1) / splits;
   const int j0 = split * span;
   const int j1 = min(min(j0 + span, max_len), pos + 1);
+  __half* kc = k_cache + (size_t)kvh * max_len * kHeadDim;  // this kv head's rows
+  __half* vc = v_cache + (size_t)kvh * max_len * kHeadDim;
 
-  extern __shared__ float sm[];  // q [group][64], k_new [64], v_new [64]
+  // Rows below pos were written by earlier steps, which have completed: when this CTA's
+  // positions fit one block of 32, fetch its key row (one per lane) and the block's value
+  // rows (dims 2 lane, 2 lane + 1) before waiting for the previous kernel.
+  const bool one_block = span <= 32 && !bad_pos;
+  const int j = j0 + lane;
+  const int nvalid = max(0, j1 - j0);
+  uint4 kreg[8];
+  __half2 vreg[32];
+  if (one_block) {
+    if (j < j1 && j != pos) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)j * kHeadDim);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kreg[e] = kr[e];
+    }
+    const __half2* vr = reinterpret_cast<const __half2*>(vc + (size_t)j0 * kHeadDim) + lane;
+#pragma unroll
+    for (int u = 0; u < 32; ++u)
+      if (u < nvalid && j0 + u != pos) vreg[u] = vr[u * (kHeadDim / 2)];
+  }
+
+  // qkv (and, for span > 32, the new cache row) come from the kernels before this one
+  grid_dependency_wait();
+  grid_launch_dependents();
+  if (bad_pos) {  // nothing is read or written: the heads read NaN
+    if (split == 0) {
+      const __half2 nan2 = __float2half2_rn(__int_as_float(0x7fc00000));
+      reinterpret_cast<__half2*>(out + head * kHeadDim)[lane] = nan2;
+    }
+    return;
+  }
+
+  extern __shared__ float sm[];  // rotated, pre-scaled queries [group][64]; new key, value [64] each
   float* qs = sm;
   float* kn = sm + group * kHeadDim;
   float* vn = kn + kHeadDim;
-
   const float* cr = cos_t + (size_t)pos * kHeadDim;
   const float* sr = sin_t + (size_t)pos * kHeadDim;
   {  // rotate this warp's query head
-    float a = __half2float(qkv[head * kHeadDim + lane]);
-    float b = __half2float(qkv[head * kHeadDim + lane + 32]);
+    float a = __half2float(__ldcg(qkv + head * kHeadDim + lane));
+    float b = __half2float(__ldcg(qkv + head * kHeadDim + lane + 32));
     rope_pair(a, b, cr, sr, lane);
     qs[warp * kHeadDim + lane] = a * scale;
     qs[warp * kHeadDim + lane + 32] = b * scale;
   }
-  if (warp == 0) {  // the new key (rotated) and value of this kv head
+  if (warp == 0 && pos >= j0 && pos < j0 + span) {
+    // this split owns the new position: rotate the key, write key and value to the
+    // cache and keep both (as fp16 values) for the loops below
     const int kb = heads * kHeadDim + kvh * kHeadDim;
     const int vb = (heads + kv_heads) * kHeadDim + kvh * kHeadDim;
-    float a = __half2float(qkv[kb + lane]);
-    float b = __half2float(qkv[kb + lane + 32]);
+    float a = __half2float(__ldcg(qkv + kb + lane));
+    float b = __half2float(__ldcg(qkv + kb + lane + 32));
     rope_pair(a, b, cr, sr, lane);
-    const __half ah = __float2half_rn(a), bh = __float2half_rn(b);  // as the cache holds it
+    const __half ah = __float2half_rn(a), bh = __float2half_rn(b);
+    const __half va = __ldcg(qkv + vb + lane), vb2 = __ldcg(qkv + vb + lane + 32);
+    kc[(size_t)pos * kHeadDim + lane] = ah;
+    kc[(size_t)pos * kHeadDim + lane + 32] = bh;
+    vc[(size_t)pos * kHeadDim + lane] = va;
+    vc[(size_t)pos * kHeadDim + lane + 32] = vb2;
     kn[lane] = __half2float(ah);
     kn[lane + 32] = __half2float(bh);
-    vn[lane] = __half2float(qkv[vb + lane]);
-    vn[lane + 32] = __half2float(qkv[vb + lane + 32]);
-    if (pos >= j0 && pos < j0 + span) {  // this split owns the new position
-      __half* kd = k_cache + ((size_t)kvh * max_len + pos) * kHeadDim;
-      __half* vd = v_cache + ((size_t)kvh * max_len + pos) * kHeadDim;
-      kd[lane] = ah;
-      kd[lane + 32] = bh;
-      vd[lane] = qkv[vb + lane];
-      vd[lane + 32] = qkv[vb + lane + 32];
-    }
+    vn[lane] = __half2float(va);
+    vn[lane + 32] = __half2float(vb2);
   }
-  __syncthreads();
+  __syncthreads();  // queries, the new row and the cache write are visible to the CTA
 
-  // partial softmax over [j0, j1): lane handles positions j0 + lane, j0 + lane + 32, ...
-  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;  // o: dims lane, lane + 32
+  // Partial softmax over [j0, j1): lane handles position jb + lane of each block of 32
+  // for the scores, and dims (2 lane, 2 lane + 1) of the output.
+  float m = -INFINITY, l = 0.f;
+  float2 o = make_float2(0.f, 0.f);
   const float* q = qs + warp * kHeadDim;
-  for (int jb = j0; jb < j1; jb += 32) {
-    const int j = jb + lane;
-    float sc = -INFINITY;
-    if (j < j1) {
-      float d = 0.f;
-      if (j == pos) {
-#pragma unroll 8
-        for (int e = 0; e < kHeadDim; ++e) d = fmaf(q[e], kn[e], d);
-      } else {
-        const __half* kr = k_cache + ((size_t)kvh * max_len + j) * kHeadDim;
+  auto score = [&](const uint4* kv) {
+    float d = 0.f;
 #pragma unroll
-        for (int e = 0; e < kHeadDim; e += 8) {
-          const uint4 kv = ldg128(kr + e);
-          const uint32_t w4[4] = {kv.x, kv.y, kv.z, kv.w};
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t w4[4] = {kv[e].x, kv[e].y, kv[e].z, kv[e].w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
-            d = fmaf(q[e + 2 * i], f.x, d);
-            d = fmaf(q[e + 2 * i + 1], f.y, d);
-          }
-        }
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+        d = fmaf(q[e * 8 + 2 * i], f.x, d);
+        d = fmaf(q[e * 8 + 2 * i + 1], f.y, d);
       }
-      sc = d;
     }
-    const float mb = warp_max(sc);
-    const float mn = fmaxf(m, mb);
+    return d;
+  };
+  auto softmax_block = [&](float sc) {  // running max / sum update over a block; returns p_j
+    const float mn = fmaxf(m, warp_max(sc));
     const float corr = m == -INFINITY ? 0.f : __expf(m - mn);
     const float pj = sc == -INFINITY ? 0.f : __expf(sc - mn);
     l = l * corr + warp_sum(pj);
-    o0 *= corr;
-    o1 *= corr;
-    const int nvalid = min(32, j1 - jb);
-    for (int u = 0; u < nvalid; ++u) {  // o += p_u * v_u
-      const float pu = __shfl_sync(0xffffffffu, pj, u);
-      const int ju = jb + u;
-      float v0, v1;
-      if (ju == pos) {
-        v0 = vn[lane];
-        v1 = vn[lane + 32];
-      } else {
-        const __half* vr = v_cache + ((size_t)kvh * max_len + ju) * kHeadDim;
-        v0 = __half2float(vr[lane]);
-        v1 = __half2float(vr[lane + 32]);
-      }
-      o0 = fmaf(pu, v0, o0);
-      o1 = fmaf(pu, v1, o1);
-    }
+    o.x *= corr;
+    o.y *= corr;
     m = mn;
+    return pj;
+  };
+  if (one_block) {
+    float sc = -INFINITY;
+    if (j < j1) {
+      if (j == pos) {
+        float d = 0.f;
+#pragma unroll 8
+        for (int e = 0; e < kHeadDim; ++e) d = fmaf(q[e], kn[e], d);
+        sc = d;
+      } else {
+        sc = score(kreg);
+      }
+    }
+    const float pj = softmax_block(sc);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      if (u < nvalid) {
+        const float pu = __shfl_sync(0xffffffffu, pj, u);
+        const float2 v = j0 + u == pos ? make_float2(vn[2 * lane], vn[2 * lane + 1]) : __half22float2(vreg[u]);
+        o.x = fmaf(pu, v.x, o.x);
+        o.y = fmaf(pu, v.y, o.y);
+      }
+    }
+  } else {
+    for (int jb = j0; jb < j1; jb += 32) {
+      const int jj = jb + lane;
+      float sc = -INFINITY;
+      if (jj < j1) {
+        const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)jj * kHeadDim);
+        uint4 kv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kv[e] = kr[e];
+        sc = score(kv);
+      }
+      const float pj = softmax_block(sc);
+      const __half2* vr = reinterpret_cast<const __half2*>(vc + (size_t)jb * kHeadDim) + lane;
+      const int nv = min(32, j1 - jb);
+#pragma unroll
+      for (int u = 0; u < 32; ++u)  // all value rows of the block in flight first
+        if (u < nv) vreg[u] = vr[u * (kHeadDim / 2)];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        if (u < nv) {
+          const float pu = __shfl_sync(0xffffffffu, pj, u);
+          const float2 v = __half22float2(vreg[u]);
+          o.x = fmaf(pu, v.x, o.x);
+          o.y = fmaf(pu, v.y, o.y);
+        }
+      }
+    }
   }
 
   // publish (m, l, o) for (head, split); the last split of this kv head combines
-  float* part = scratch + ((size_t)head * splits + split) * (kHeadDim + 2);
+  constexpr int kPart = kHeadDim + 2;
+  float* part = scratch + ((size_t)head * splits + split) * kPart;
   if (lane == 0) {
     part[0] = m;
     part[1] = l;
   }
-  part[2 + lane] = o0;
-  part[2 + lane + 32] = o1;
+  reinterpret_cast<float2*>(part + 2)[lane] = o;
   __threadfence();
   __syncthreads();
-  unsigned* counters = reinterpret_cast<unsigned*>(scratch + (size_t)heads * splits * (kHeadDim + 2));
+  unsigned* counters = reinterpret_cast<unsigned*>(scratch + (size_t)heads * splits * kPart);
   __shared__ unsigned prev;
   if (threadIdx.x == 0) prev = atomicAdd(counters + kvh, 1u);
   __syncthreads();
   if (prev != (unsigned)(splits - 1)) return;
   __threadfence();
+  // Combine the splits in split order, 32 at a time: lane s holds split s's max and
+  // weight; each lane gathers its two dims of every split's output.
+  const float* ph = scratch + (size_t)head * splits * kPart;
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s)
-    M = fmaxf(M, __ldcg(scratch + ((size_t)head * splits + s) * (kHeadDim + 2)));
-  float L = 0.f, a0 = 0.f, a1 = 0.f;
-  for (int s = 0; s < splits; ++s) {
-    const float* ps = scratch + ((size_t)head * splits + s) * (kHeadDim + 2);
-    const float ms = __ldcg(ps);
-    if (ms == -INFINITY) continue;
-    const float w = __expf(ms - M);
-    L = fmaf(__ldcg(ps + 1), w, L);
-    a0 = fmaf(__ldcg(ps + 2 + lane), w, a0);
-    a1 = fmaf(__ldcg(ps + 2 + lane + 32), w, a1);
+  for (int s = lane; s < splits; s += 32) M = fmaxf(M, __ldcg(ph + (size_t)s * kPart));
+  M = warp_max(M);
+  float L = 0.f;
+  float2 a = make_float2(0.f, 0.f);
+  for (int s0 = 0; s0 < splits; s0 += 32) {
+    const int s = s0 + lane;
+    float w = 0.f, lw = 0.f;
+    if (s < splits) {
+      const float ms = __ldcg(ph + (size_t)s * kPart);
+      w = ms == -INFINITY ? 0.f : __expf(ms - M);
+      lw = __ldcg(ph + (size_t)s * kPart + 1) * w;
+    }
+    float2 os[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u)
+      if (s0 + u < splits) os[u] = __ldcg(reinterpret_cast<const float2*>(ph + (size_t)(s0 + u) * kPart + 2) + lane);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      const float wu = __shfl_sync(0xffffffffu, w, u);
+      const float lu = __shfl_sync(0xffffffffu, lw, u);
+      if (s0 + u < splits) {
+        L += lu;
+        a.x = fmaf(os[u].x, wu, a.x);
+        a.y = fmaf(os[u].y, wu, a.y);
+      }
+    }
   }
-  out[head * kHeadDim + lane] = __float2half_rn(a0 / L);
-  out[head * kHeadDim + lane + 32] = __float2half_rn(a1 / L);
+  reinterpret_cast<__half2*>(out + head * kHeadDim)[lane] = __floats2half2_rn(a.x / L, a.y / L);
   __syncthreads();
   if (threadIdx.x == 0) counters[kvh] = 0u;
 }
@@ -204,14 +274,18 @@ size_t decode_attention_scratch_bytes(int heads, int kv_heads, int splits) {
 int launch_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
                             const long long* pos, void* k_cache, void* v_cache, void* out,
                             void* scratch, int heads, int kv_heads, int head_dim, int max_len,
-                            int splits, cudaStream_t stream) {
+                            int splits, bool pdl, cudaStream_t stream) {
   const int group = heads / kv_heads;
   const size_t smem = (size_t)(group + 2) * kHeadDim * 4;
-  k_decode_attention<<<kv_heads * splits, 32 * group, smem, stream>>>(
+  // up to 8 query heads per kv head (256 threads) the prefetch keeps its registers;
+  // larger groups run with the register cap of 1024-thread blocks
+  auto kernel = group <= 8 ? k_decode_attention<256> : k_decode_attention<1024>;
+  cudaError_t e = launch_maybe_pdl(
+      kernel, dim3(kv_heads * splits), dim3(32 * group), smem, stream, pdl,
       static_cast<const __half*>(qkv), cos_t, sin_t, pos, static_cast<__half*>(k_cache),
       static_cast<__half*>(v_cache), static_cast<__half*>(out), static_cast<float*>(scratch), heads,
-      kv_heads, max_len, splits, rsqrtf((float)head_dim));
-  const cudaError_t e = cudaGetLastError();
+      kv_heads, max_len, splits, 1.0f / sqrtf((float)head_dim));
+  (void)cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("k_decode_attention launch failed: %s", cudaGetErrorString(e));
     return W4A16_ERR_CUDA;

@@ -144,10 +144,38 @@ __device__ __forceinline__ uint4 ldg128(const void* p) {
   return v;
 }
 
+// 16-byte load through L2 only: for data that another kernel may have written while
+// this one was already running (programmatic dependent launch), where the
+// non-coherent path is not allowed.
+__device__ __forceinline__ uint4 ldcg128(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// Two floats rounded to fp16 (round to nearest even), packed low | high.
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(lo)) |
+         ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+}
+
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while the
+// previous kernel in the stream is still running.  grid_dependency_wait() returns once
+// that kernel has completed and its memory is visible (at once for a normal launch);
+// grid_launch_dependents() lets the next such kernel be scheduled.  Kernels here call
+// the trigger only after their own wait, so at most two consecutive kernels overlap.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ----------------------------------------------------------------- mbarrier

@@ -109,7 +109,22 @@ enum XMode : int { kXGlobal = 0, kXCopy = 1, kXRmsNorm = 2, kXSwiGlu = 3 };
 //                  workspace needed).
 //   kSchedDynamic  warps pull whole tiles from an atomic counter in the workspace, so
 //                  SMs that stream faster take more tiles.  Best for many tiles.
-enum Sched : int { kSchedStreamK = 0, kSchedStatic = 1, kSchedDynamic = 2 };
+//   kSchedLocal    every CTA takes an equal contiguous range of whole tiles and its
+//                  warps split that range's units (at most STAGES each, so every copy
+//                  is issued at the start); tiles shared by warps are reduced in shared
+//                  memory.  No workspace, no atomics: for the small matrices of a decode
+//                  step, whose time is latency rather than bandwidth.
+enum Sched : int { kSchedStreamK = 0, kSchedStatic = 1, kSchedDynamic = 2, kSchedLocal = 3 };
+
+// 8-element chunks of the staged vector per thread (K <= kStageChunks * 8 * threads).
+constexpr int kStageChunks = 6;
+
+// Units one CTA can hold under kSchedLocal, and the shared memory of their partial sums.
+template <int WARPS, int STAGES, int ROWS>
+struct LocalPlan {
+  static constexpr int kUnits = WARPS * STAGES;
+  static constexpr int kBytes = kUnits * ROWS * 4;
+};
 
 // Shared-memory stage of one warp: a window of SLABS 256-column slabs of RT*16 rows,
 // one 3-D TMA box laid out [row][slab][128 B] with the 128-byte swizzle (1024-byte
@@ -298,74 +313,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int g = lane >> 2;  // MMA group id: rows g and g+8 of each 16-row block
   const int t = lane & 3;   // thread in group: 32-column chunk t of each 128-column group
 
-  // XS: the CTA first writes the activation vector into shared memory (fragment
-  // order, see xs_offset), copying it or computing it from the prologue source;
-  // every B fragment is then one shared-memory load.
+  // XS: the CTA writes the activation vector into shared memory (fragment order,
+  // see xs_offset), copying it or computing it from the prologue source; every B
+  // fragment is then one shared-memory load.  The staging comes after the first
+  // weight copies are in flight.
   constexpr bool XS = XM != kXGlobal;
   using Plan = SmemPlan<WARPS, STAGES, L>;
   const uint32_t xs = base + (uint32_t)Plan::kXOff;
-  if (XS) {
-    uint8_t* xsp = smem_raw + (xs - smem_addr(smem_raw));
-    const int nch = p.K >> 3;
-    if (XM == kXCopy) {
-      for (int c = threadIdx.x; c < nch; c += blockDim.x)
-        *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = ldg128(p.x + c * 8);
-    } else if (XM == kXRmsNorm) {
-      const float* h = static_cast<const float*>(p.pro_src);
-      float ss = 0.f;
-      for (int i = threadIdx.x; i < p.K; i += blockDim.x) {
-        const float v = __ldg(h + i);
-        ss = fmaf(v, v, ss);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      float* red = reinterpret_cast<float*>(xsp + (size_t)p.K * 2);  // WARPS partial sums
-      if (lane == 0) red[warp] = ss;
-      __syncthreads();
-      float tot = 0.f;
-      for (int w = 0; w < WARPS; ++w) tot += red[w];
-      const float r = rsqrtf(tot / (float)p.K + p.pro_eps);
-      for (int c = threadIdx.x; c < nch; c += blockDim.x) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int k = c * 8 + 2 * i;
-          const float a = __ldg(h + k) * r * __ldg(p.pro_gamma + k);
-          const float b = __ldg(h + k + 1) * r * __ldg(p.pro_gamma + k + 1);
-          pk[i] = (uint32_t)__half_as_ushort(__float2half_rn(a)) |
-                  ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
-        }
-        *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-    } else if (XM == kXSwiGlu) {
-      const __half* gu = static_cast<const __half*>(p.pro_src);
-      for (int c = threadIdx.x; c < nch; c += blockDim.x) {
-        const uint4 gv = ldg128(gu + c * 8);
-        const uint4 uv = ldg128(gu + p.K + c * 8);
-        const uint32_t gw4[4] = {gv.x, gv.y, gv.z, gv.w};
-        const uint32_t uw4[4] = {uv.x, uv.y, uv.z, uv.w};
-        uint32_t pk[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gw4[i]));
-          const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uw4[i]));
-          const float a = g2.x / (1.0f + expf(-g2.x)) * u2.x;
-          const float b = g2.y / (1.0f + expf(-g2.y)) * u2.y;
-          pk[i] = (uint32_t)__half_as_ushort(__float2half_rn(a)) |
-                  ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
-        }
-        *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-    }
-    __syncthreads();
-  }
 
-  const int gw = warp * gridDim.x + blockIdx.x;  // warp-major: ranges spread over all SMs
-  if (gw >= p.nwarps) return;
+  const bool local = p.sched == kSchedLocal;
   const int ks = p.kslabs;
   const int nwin = p.nwin;
-  const long long U = p.units;
-  const int T = p.nwarps;
+  // kSchedLocal: this CTA's tiles [tb0, tb0 + ntl) and their units, split over its warps
+  const int tb0 = (int)((long long)blockIdx.x * p.ntiles / gridDim.x);
+  const int ntl = local ? (int)((long long)(blockIdx.x + 1) * p.ntiles / gridDim.x) - tb0 : 0;
+  const int gw = local ? warp : warp * gridDim.x + blockIdx.x;  // warp-major: ranges spread over all SMs
+  const long long U = local ? (long long)ntl * nwin : p.units;
+  const int T = local ? WARPS : p.nwarps;
+  const bool active = gw < T;
   const bool dyn = p.sched == kSchedDynamic;
   unsigned* next_tile = p.counters + kNextTileCounter;
   auto pull_tile = [&]() -> int {  // dynamic scheduling: the next unclaimed tile
@@ -380,13 +345,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   } else if (p.sched == kSchedStreamK) {
     u0 = (long long)gw * U / T;
     u1 = (long long)(gw + 1) * U / T;
+  } else if (local) {  // units counted from the CTA's first tile
+    u0 = (long long)tb0 * nwin + (long long)gw * U / T;
+    u1 = (long long)tb0 * nwin + (long long)(gw + 1) * U / T;
   } else {
-    u0 = (long long)pull_tile() * nwin;
+    u0 = active ? (long long)pull_tile() * nwin : U;
     u1 = u0 < U ? U : u0;  // bounded below by the tiles actually pulled
   }
   const int first_tile = (int)(u0 / nwin);
   const int first_win = (int)(u0 - (long long)first_tile * nwin);
-  const int count = (int)(u1 - u0);
+  const int count = active ? (int)(u1 - u0) : 0;
 
   const uint32_t wring = base + (uint32_t)(warp * STAGES * L::kWStride);
   const uint32_t sring = base + (uint32_t)(Plan::kScaleOff + warp * STAGES * L::kSStride);
@@ -439,6 +407,104 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll 1
   for (int s = 0; s < STAGES; ++s) issue_one();
 
+  // Everything above touches only the weights and this call's workspace.  Under a
+  // programmatic dependent launch the previous kernel may still be running: wait for
+  // it before reading the activation, the bias or anything it wrote, then let the
+  // next kernel be scheduled (it will overlap this one's tail).
+  grid_dependency_wait();
+  grid_launch_dependents();
+
+  // kSchedLocal partial sums [unit of the CTA][16 rows] sit after the staged vector;
+  // slots no segment starts at stay zero
+  float* lpart = reinterpret_cast<float*>(smem_raw + (xs - smem_addr(smem_raw)) +
+                                          (XS ? (size_t)p.K * 2 + 128 : 0));
+  if (local) {
+    for (int i = threadIdx.x; i < LocalPlan<WARPS, STAGES, kRows>::kUnits * kRows; i += blockDim.x)
+      lpart[i] = 0.f;
+    if (!XS) __syncthreads();
+  }
+
+  if (XS) {
+    // x, h, gate|up and the bias may have been written by the previous kernel:
+    // read them through L2 (ldcg), not the non-coherent path.
+    uint8_t* xsp = smem_raw + (xs - smem_addr(smem_raw));
+    const int nch = p.K >> 3;  // 8-element chunks; thread i takes chunks i, i + blockDim, ...
+    // Every loop below is unrolled over kStageChunks chunks per thread with a guard, so a
+    // thread's loads are all in flight together (the host stages only K <= kStageChunks *
+    // threads * 8).
+    if (XM == kXCopy) {
+#pragma unroll
+      for (int j = 0; j < kStageChunks; ++j) {
+        const int c = threadIdx.x + j * WARPS * 32;
+        if (c < nch) *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = ldcg128(p.x + c * 8);
+      }
+    } else if (XM == kXRmsNorm) {
+      const float4* h4 = static_cast<const float4*>(p.pro_src);
+      const float4* g4 = reinterpret_cast<const float4*>(p.pro_gamma);
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < kStageChunks; ++j) {
+        const int c = threadIdx.x + j * WARPS * 32;
+        if (c < nch) {
+          const float4 a = __ldcg(h4 + 2 * c), b = __ldcg(h4 + 2 * c + 1);
+          ss = fmaf(a.x, a.x, ss);
+          ss = fmaf(a.y, a.y, ss);
+          ss = fmaf(a.z, a.z, ss);
+          ss = fmaf(a.w, a.w, ss);
+          ss = fmaf(b.x, b.x, ss);
+          ss = fmaf(b.y, b.y, ss);
+          ss = fmaf(b.z, b.z, ss);
+          ss = fmaf(b.w, b.w, ss);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      float* red = reinterpret_cast<float*>(xsp + (size_t)p.K * 2);  // WARPS partial sums
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) tot += red[w];
+      const float r = rsqrtf(tot / (float)p.K + p.pro_eps);
+#pragma unroll
+      for (int j = 0; j < kStageChunks; ++j) {
+        const int c = threadIdx.x + j * WARPS * 32;
+        if (c < nch) {
+          const float4 a = __ldcg(h4 + 2 * c), b = __ldcg(h4 + 2 * c + 1);
+          const float4 ga = __ldg(g4 + 2 * c), gb = __ldg(g4 + 2 * c + 1);
+          const uint32_t p0 = pack_half2(a.x * r * ga.x, a.y * r * ga.y);
+          const uint32_t p1 = pack_half2(a.z * r * ga.z, a.w * r * ga.w);
+          const uint32_t p2 = pack_half2(b.x * r * gb.x, b.y * r * gb.y);
+          const uint32_t p3 = pack_half2(b.z * r * gb.z, b.w * r * gb.w);
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(p0, p1, p2, p3);
+        }
+      }
+    } else if (XM == kXSwiGlu) {
+      const __half* gu = static_cast<const __half*>(p.pro_src);
+#pragma unroll
+      for (int j = 0; j < kStageChunks; ++j) {
+        const int c = threadIdx.x + j * WARPS * 32;
+        if (c < nch) {
+          const uint4 gv = ldcg128(gu + c * 8);
+          const uint4 uv = ldcg128(gu + p.K + c * 8);
+          const uint32_t gw4[4] = {gv.x, gv.y, gv.z, gv.w};
+          const uint32_t uw4[4] = {uv.x, uv.y, uv.z, uv.w};
+          uint32_t pk[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gw4[i]));
+            const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uw4[i]));
+            pk[i] = pack_half2(g2.x / (1.0f + expf(-g2.x)) * u2.x, g2.y / (1.0f + expf(-g2.y)) * u2.y);
+          }
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  if (!active && !local) return;
+
   float tot[RT][NH][4];
   float acc[RT][2][NH][4];
   float srow[RT][2];
@@ -480,6 +546,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       record_device_error(kDevErrStageTimeout);
       for (int s = consumed + 1; s < issued; ++s)
         mbar_wait_bounded(bar0 + 8 * (s % STAGES), (s / STAGES) & 1u, kDrainWaitLimitNs);
+      if (local) break;  // the CTA still meets at the reduction barrier
       return;
     }
     const uint32_t wbase = wring + slot * L::kWStride;
@@ -529,9 +596,22 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             const bool ok = NB == 1 ? (t == 0 && (i & 1) == 0) : (n < p.M);
             if (ok && r < p.N) {
               float v = tot[rt][h][i];
-              if (p.bias) v += __ldg(p.bias + r);
+              if (p.bias) v += __ldcg(p.bias + r);  // may be the previous kernel's output
               static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
             }
+          }
+      continue;
+    }
+    if (local) {  // segment of a tile shared within the CTA: its partial goes to smem
+      float* lp = lpart + ((cur_tile - tb0) * nwin + tile_w0) * kRows;
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const bool ok = NB == 1 && t == 0 && (i & 1) == 0;
+            if (ok) lp[rt * 16 + g + (i < 2 ? 0 : 8)] = tot[rt][h][i];
           }
       continue;
     }
@@ -578,12 +658,30 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             const size_t wstride = (size_t)2 * p.M * kRows;
             float v = __ldcg(p.partial + ((size_t)w_first * 2 + slot_first) * p.M * kRows + off);
             for (int w = w_first + 1; w <= w_last; ++w) v += __ldcg(p.partial + (size_t)w * wstride + off);
-            if (p.bias) v += __ldg(p.bias + r);
+            if (p.bias) v += __ldcg(p.bias + r);  // may be the previous kernel's output
             static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
           }
         }
     __syncwarp();
     if (lane == 0) p.counters[w_first] = 0u;  // leave the workspace zeroed
+  }
+  if (local) {
+    // Tiles split between warps of this CTA: add their segments in window order.
+    if constexpr (NB == 1) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < ntl * kRows; i += blockDim.x) {
+        const int tl = i / kRows, rl = i - tl * kRows;
+        const long long tu0 = (long long)tl * nwin;
+        if (warp_of_unit(tu0, U, T) == warp_of_unit(tu0 + nwin - 1, U, T)) continue;  // written
+        const int r = (tb0 + tl) * kRows + rl;
+        if (r >= p.N) continue;
+        float v = 0.f;
+        for (int w = 0; w < nwin; ++w) v += lpart[(tl * nwin + w) * kRows + rl];
+        if (p.bias) v += __ldcg(p.bias + r);
+        static_cast<OT*>(p.y)[r] = from_f32<OT>(v);
+      }
+    }
+    return;
   }
   if (dyn && lane == 0) {
     // Every warp has made its last pull before it counts itself done, so the last
@@ -748,7 +846,8 @@ template <int PACK, int GS, typename ST, int NB, typename OT, int XM>
 int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
   using L = StageLayout<kSlabs, kRT, GS, ST>;
   auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM>;
-  const int smem = tma_smem_bytes<GS, ST>() + (XM != kXGlobal ? p.K * 2 + 128 : 0);
+  const int smem_base = tma_smem_bytes<GS, ST>() + (XM != kXGlobal ? p.K * 2 + 128 : 0);
+  int smem = smem_base;
   if (smem > di.smem_optin) {
     set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
     return W4A16_ERR_SHAPE;
@@ -822,27 +921,42 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   const size_t need = kCounterBytes + (size_t)tk * 2 * M * kTileRows * 4;
   const bool have_ws = p.split_k != 1 && tk <= kMaxWarps - 2 && p.workspace &&
                        p.workspace_bytes >= need && aligned(p.workspace, 256);
-  if (!have_ws)
+  // kSchedLocal when every CTA's share of whole tiles fits its warps' rings at once
+  using LP = LocalPlan<kWarps, kStages, kTileRows>;
+  const int g_local = prm.ntiles < di.sms ? prm.ntiles : di.sms;
+  const long long tiles_per_cta = (prm.ntiles + g_local - 1) / (g_local > 0 ? g_local : 1);
+  const bool local_ok = NB == 1 && M == 1 && p.split_k != 1 && g_local > 0 &&
+                        tiles_per_cta * prm.nwin <= LP::kUnits && smem_base + LP::kBytes <= di.smem_optin;
+  if (local_ok)
+    prm.sched = kSchedLocal;
+  else if (!have_ws)
     prm.sched = kSchedStatic;
   else if (prm.ntiles * 4 >= slots || prm.nwin <= 2)
     prm.sched = kSchedDynamic;
   else
     prm.sched = kSchedStreamK;
-  prm.nwarps = (int)(prm.sched == kSchedStreamK ? tk : tt);
+  prm.nwarps = (int)(prm.sched == kSchedStreamK ? tk : prm.sched == kSchedLocal ? g_local * kWarps : tt);
+  if (prm.sched == kSchedLocal) smem = smem_base + LP::kBytes;
   prm.pro_src = p.pro_src;
   prm.pro_gamma = p.pro_gamma;
   prm.pro_eps = p.pro_eps;
   prm.partial = nullptr;
   prm.counters = nullptr;
-  if (have_ws) {
+  if (have_ws && prm.sched != kSchedLocal) {
     uint8_t* ws = static_cast<uint8_t*>(p.workspace);
     prm.counters = reinterpret_cast<unsigned*>(ws);
     prm.partial = reinterpret_cast<float*>(ws + kCounterBytes);
   }
-  int grid = prm.nwarps < di.sms ? prm.nwarps : di.sms;
+  int grid = prm.sched == kSchedLocal ? g_local : prm.nwarps < di.sms ? prm.nwarps : di.sms;
   if (grid < 1) grid = 1;
-  kernel<<<grid, kWarps * 32, smem, p.stream>>>(wmap, smap, prm);
-  return check_launch("k_gemv_tma");
+  const cudaError_t le = launch_maybe_pdl(kernel, dim3(grid), dim3(kWarps * 32), (size_t)smem, p.stream,
+                                          p.pdl, wmap, smap, prm);
+  (void)cudaGetLastError();  // the status is `le`; do not leave it for a later check
+  if (le != cudaSuccess) {
+    set_error("k_gemv_tma launch failed: %s", cudaGetErrorString(le));
+    return W4A16_ERR_CUDA;
+  }
+  return W4A16_OK;
 }
 
 template <int PACK, int GS, typename ST, typename OT>
@@ -865,9 +979,9 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
       (PACK == W4A16_PACK_INTERLEAVED ||
        (GS == 0 && std::is_same<ST, float>::value && std::is_same<OT, float>::value)) &&
       StageLayout<kSlabs, kRT, GS, ST>::kScaleBoxOk;
-  if (p.prologue != W4A16_PROLOGUE_NONE && (!kTmaVariant || !use_tma)) {
-    set_error("fused prologue needs the TMA path: cols %% 256 == 0, 16-byte aligned weights, "
-              "interleaved packing");
+  if (p.staged && (!kTmaVariant || !use_tma)) {
+    set_error("the staged (fused) GEMV needs the TMA path: cols %% 256 == 0, 16-byte aligned "
+              "weights, interleaved packing");
     return W4A16_ERR_SHAPE;
   }
   if constexpr (!kTmaVariant) {
@@ -877,18 +991,22 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
     return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
   } else {
   if (!use_tma) return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
-  const bool xs_fits = tma_smem_bytes<GS, ST>() + p.K * 2 + 128 <= di.smem_optin;
-  if (p.prologue != W4A16_PROLOGUE_NONE) {
+  const bool xs_fits = tma_smem_bytes<GS, ST>() + p.K * 2 + 128 <= di.smem_optin &&
+                       p.K <= kStageChunks * 8 * kWarps * 32;
+  if (p.staged) {
     if (M != 1 || !xs_fits) {
-      set_error("fused prologue needs one activation vector and cols <= %d", (di.smem_optin - tma_smem_bytes<GS, ST>() - 128) / 2);
+      set_error("the staged (fused) GEMV needs one activation vector and cols <= %d",
+                (di.smem_optin - tma_smem_bytes<GS, ST>() - 128) / 2);
       return W4A16_ERR_SHAPE;
     }
     if constexpr (PACK == W4A16_PACK_INTERLEAVED) {
       if (p.prologue == W4A16_PROLOGUE_RMSNORM)
         return launch_tma<PACK, GS, ST, 1, OT, kXRmsNorm>(p, x, M, y, di, dev);
-      return launch_tma<PACK, GS, ST, 1, OT, kXSwiGlu>(p, x, M, y, di, dev);
+      if (p.prologue == W4A16_PROLOGUE_SWIGLU)
+        return launch_tma<PACK, GS, ST, 1, OT, kXSwiGlu>(p, x, M, y, di, dev);
+      return launch_tma<PACK, GS, ST, 1, OT, kXCopy>(p, x, M, y, di, dev);
     }
-    set_error("fused prologues take the interleaved packing");
+    set_error("the staged (fused) GEMV takes the interleaved packing");
     return W4A16_ERR_DTYPE;
   }
   if (M == 1) {

@@ -1,10 +1,13 @@
 // Internal (C++) interface between the C-ABI layer (w4a16_capi.cu) and the kernel
-// launchers (w4a16_kernels.cu).  Nothing here crosses the library boundary.
+// launchers (w4a16_gemv.cu, w4a16_aux.cu, w4a16_decode.cu).  Nothing here crosses the
+// library boundary.
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
+
+#include <utility>
 
 #include "w4a16_b200.h"
 
@@ -30,6 +33,8 @@ struct GemvProblem {
   const void* pro_src = nullptr;
   const float* pro_gamma = nullptr;
   float pro_eps = 0.f;
+  bool staged = false;              // fused entry: x staged in shared memory, TMA kernel only
+  bool pdl = false;                 // programmatic dependent launch (staged GEMV only)
   cudaStream_t stream = nullptr;
 };
 
@@ -67,7 +72,26 @@ size_t decode_attention_scratch_bytes(int heads, int kv_heads, int splits);
 int launch_decode_attention(const void* qkv, const float* cos_t, const float* sin_t,
                             const long long* pos, void* k_cache, void* v_cache, void* out,
                             void* scratch, int heads, int kv_heads, int head_dim, int max_len,
-                            int splits, cudaStream_t stream);
+                            int splits, bool pdl, cudaStream_t stream);
+
+// Launch `kernel` with programmatic stream serialisation when `pdl` is set (the kernel
+// may start while the previous one in the stream is still running; it must call
+// grid_dependency_wait() before touching that kernel's outputs), normally otherwise.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Reads (and clears) the device-side error word written by kernels whose bounded
 // waits ran out.  Synchronises `stream`.

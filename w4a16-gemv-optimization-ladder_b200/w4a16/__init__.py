@@ -9,6 +9,7 @@ from .kernels import (
     dequant_int4,
     gemv,
     gemv_rmsnorm,
+    gemv_staged,
     gemv_swiglu,
     matvec_byte,
     matvec_champ,
@@ -19,6 +20,7 @@ from .kernels import (
     matvec_uint4,
     quantize_pack,
     read_device_error,
+    new_workspace,
     reserve_workspace,
     w4a16_gemv,
     w4a16_gemv_g128,
@@ -41,6 +43,7 @@ __all__ = [
     "quantize_int4_symmetric", "quantize_int4_group", "pack_int4", "pack_int4_interleaved",
     "dequant_ref", "dequant_ref_group", "W4A16Linear", "replace_linear_with_w4a16",
     # additions
-    "gemv", "gemv_rmsnorm", "gemv_swiglu", "decode_attention", "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace",
+    "gemv", "gemv_staged", "gemv_rmsnorm", "gemv_swiglu", "decode_attention", "new_workspace",
+    "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace",
     "read_device_error",
 ]

@@ -17,11 +17,14 @@ DTYPE_F32 = 0
 DTYPE_F16 = 1
 PACK_INTERLEAVED = 0
 PACK_SIMPLE = 1
+PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
 PROLOGUE_SWIGLU = 2
+LAUNCH_PDL = 1
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
+_u = ctypes.c_uint
 _sz = ctypes.c_size_t
 
 _REF_SIG = [_p, _p, _p, _p, _i, _i, _p]
@@ -38,8 +41,9 @@ SIGNATURES = {
     "w4a16_fp16_cuda": ([_p, _p, _p, _i, _i, _p], _i),
     "w4a16_gemv": ([_p, _i, _p, _i, _i, _p, _i, _i, _i, _p, _i, _p, _p, _sz, _p], _i),
     "w4a16_gemv_workspace_bytes": ([_i, _i, _i], _sz),
-    "w4a16_gemv_fused": ([_p, _p, _i, _i, _i, _p, _p, ctypes.c_float, _i, _i, _p, _i, _p, _p, _sz, _p], _i),
-    "w4a16_decode_attention": ([_p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i, _i, _i, _p], _i),
+    "w4a16_gemv_fused": ([_p, _p, _i, _i, _i, _p, _p, ctypes.c_float, _i, _i, _p, _i, _p, _p, _sz, _u, _p],
+                         _i),
+    "w4a16_decode_attention": ([_p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i, _i, _i, _u, _p], _i),
     "w4a16_decode_attention_scratch_bytes": ([_i, _i, _i], _sz),
     "w4a16_gemv_noalloc": ([_p, _p, _i, _i, _p, _i, _i, _p, _p], _i),
     "w4a16_dequant": ([_p, _i, _p, _i, _i, _i, _i, _p, _p], _i),

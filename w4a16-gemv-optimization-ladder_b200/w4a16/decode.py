@@ -89,12 +89,15 @@ class _Proj:
 class W4A16LlamaDecoder:
     """Random-init Llama decoder for one-token steps (batch 1) over a static KV cache."""
 
-    def __init__(self, cfg=LLAMA_3_2_1B, device="cuda", seed=0, dense=False, std=0.02, fused=None):
+    def __init__(self, cfg=LLAMA_3_2_1B, device="cuda", seed=0, dense=False, std=0.02, fused=None,
+                 pdl=None):
         self.cfg = cfg
         self.dense = dense
         self.fused = (not dense) if fused is None else bool(fused)
         if self.fused and (dense or cfg.head_dim != 64):
             raise ValueError("the fused step needs int4 weights and head_dim 64")
+        # chained launches (each kernel starts while the previous one finishes)
+        self.pdl = self.fused if pdl is None else bool(pdl) and self.fused
         dev = torch.device(device)
         self.device = dev
         g = torch.Generator(device=dev).manual_seed(seed)
@@ -130,6 +133,8 @@ class W4A16LlamaDecoder:
         self.qkv = torch.empty(cfg.qkv_rows, dtype=torch.float16, device=dev)
         self.gu = torch.empty(2 * I, dtype=torch.float16, device=dev)
         self.attn = torch.empty(cfg.heads * D, dtype=torch.float16, device=dev)
+        # two split-K workspaces, alternated so that overlapping neighbours never share one
+        self.ws = [K.new_workspace(dev), K.new_workspace(dev)] if self.fused else None
         self.logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
         self.graph = None
 
@@ -168,18 +173,24 @@ class W4A16LlamaDecoder:
 
     def _step_fused(self):
         cfg = self.cfg
-        G = GROUP
+        G, pdl, ws = GROUP, self.pdl, self.ws
         self.h.copy_(self.embed.index_select(0, self.token).view(-1))
         for li, L in enumerate(self.layers):
             qkv, o, gu, down = L["qkv"], L["o"], L["gu"], L["down"]
-            K.gemv_rmsnorm(qkv.packed, qkv.scale, self.h, L["norm_attn"], cfg.eps, group=G, out=self.qkv)
+            # GEMVs alternate workspaces: qkv ws0, o ws1, gu ws0, down ws1 (attention has its own)
+            K.gemv_rmsnorm(qkv.packed, qkv.scale, self.h, L["norm_attn"], cfg.eps, group=G, out=self.qkv,
+                           pdl=pdl, workspace=ws[0])
             K.decode_attention(self.qkv, self.cos, self.sin, self.pos, self.k_cache[li], self.v_cache[li],
-                               heads=cfg.heads, kv_heads=cfg.kv_heads, out=self.attn)
-            K.gemv(o.packed, o.scale, self.attn, group=G, bias=self.h, out=self.h)
-            K.gemv_rmsnorm(gu.packed, gu.scale, self.h, L["norm_mlp"], cfg.eps, group=G, out=self.gu)
-            K.gemv_swiglu(down.packed, down.scale, self.gu, group=G, bias=self.h, out=self.h)
+                               heads=cfg.heads, kv_heads=cfg.kv_heads, out=self.attn, pdl=pdl)
+            K.gemv_staged(o.packed, o.scale, self.attn, group=G, bias=self.h, out=self.h, pdl=pdl,
+                          workspace=ws[1])
+            K.gemv_rmsnorm(gu.packed, gu.scale, self.h, L["norm_mlp"], cfg.eps, group=G, out=self.gu,
+                           pdl=pdl, workspace=ws[0])
+            K.gemv_swiglu(down.packed, down.scale, self.gu, group=G, bias=self.h, out=self.h, pdl=pdl,
+                          workspace=ws[1])
         head = self.lm_head
-        K.gemv_rmsnorm(head.packed, head.scale, self.h, self.norm_final, cfg.eps, group=G, out=self.logits)
+        K.gemv_rmsnorm(head.packed, head.scale, self.h, self.norm_final, cfg.eps, group=G, out=self.logits,
+                       pdl=pdl, workspace=ws[0])
         return self.logits
 
     def _step(self):
@@ -270,3 +281,49 @@ class W4A16LlamaDecoder:
             a = F.silu(gu[:cfg.intermediate]) * gu[cfg.intermediate:]
             h = h + L["down"].dequantized() @ a
         return self.lm_head.dequantized() @ norm(h, self.norm_final)
+
+
+def main(argv=None):
+    """Time one decode step (graph replay, or eager launches) of the Llama-3.2-1B
+    architecture: the counterpart of the reference's benchmarks/end_to_end.py."""
+    import argparse
+    import json
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--mode", choices=["fused", "unfused", "dense"], default="fused")
+    ap.add_argument("--no-pdl", action="store_true", help="fused mode without chained launches")
+    ap.add_argument("--layers", type=int, default=LLAMA_3_2_1B.layers)
+    ap.add_argument("--max-len", type=int, default=LLAMA_3_2_1B.max_len)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--eager", action="store_true", help="launch op by op (no CUDA graph)")
+    a = ap.parse_args(argv)
+    cfg = LlamaDecodeConfig(layers=a.layers, max_len=a.max_len)
+    dec = W4A16LlamaDecoder(cfg, dense=a.mode == "dense", fused=a.mode == "fused",
+                            pdl=False if a.no_pdl else None)
+    pos = cfg.max_len - 1
+    dec.fill_cache(pos)
+    dec.token.fill_(1)
+    dec.pos.fill_(pos)
+    if a.eager:
+        run = dec._step
+    else:
+        dec.capture()
+        run = dec.graph.replay
+    for _ in range(a.warmup):
+        run()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(a.steps):
+        run()
+    en.record()
+    torch.cuda.synchronize()
+    us = st.elapsed_time(en) * 1000.0 / max(a.steps, 1)
+    print(json.dumps({"mode": a.mode, "pdl": dec.pdl, "graph": not a.eager, "layers": cfg.layers,
+                      "kv_len": pos + 1, "step_us": round(us, 2), "weight_bytes": dec.weight_bytes(),
+                      "weight_gbs": round(dec.weight_bytes() / us / 1e3, 1)}))
+
+
+if __name__ == "__main__":
+    main()

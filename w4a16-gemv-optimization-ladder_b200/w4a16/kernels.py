@@ -71,7 +71,7 @@ _WORKSPACE = {}
 
 
 def _workspace(device, batch, rows, cols):
-    """Per-device zero-filled buffer for the split-K path (the kernels leave it zeroed).
+    """Per-device zero-filled buffer for the split-K path (the kernels re-zero its counters).
 
     Grown outside stream capture only; during capture a too-small buffer just turns
     split-K off for that call."""
@@ -89,6 +89,15 @@ def _workspace(device, batch, rows, cols):
 def reserve_workspace(device, batch, rows, cols):
     """Grow the split-K workspace ahead of CUDA-graph capture."""
     _workspace(torch.device(device), batch, rows, cols)
+
+
+def new_workspace(device, batch=1):
+    """A zero-filled workspace of its own for the split-K path (any rows and cols).
+
+    Chained launches (pdl=True) overlap two consecutive kernels, so consecutive calls
+    must use different workspaces; alternate two of these."""
+    need = int(_lib.lib().w4a16_gemv_workspace_bytes(batch, 1, 1))
+    return torch.zeros(need, dtype=torch.uint8, device=torch.device(device))
 
 
 # --------------------------------------------------------------- general entry
@@ -135,7 +144,8 @@ def gemv(packed, scale, x, *, group=0, packing="interleaved", bias=None, out_dty
     return out
 
 
-def _fused(prologue, packed, scale, src, gamma, eps, group, bias, out, out_dtype, split_k):
+def _fused(prologue, packed, scale, src, gamma, eps, group, bias, out, out_dtype, split_k, pdl,
+           workspace):
     _check_packed(packed)
     rows, cols = packed.shape[0], packed.shape[1] * 2
     dev = packed.device
@@ -149,18 +159,43 @@ def _fused(prologue, packed, scale, src, gamma, eps, group, bias, out, out_dtype
     if bias is not None:
         _need(bias.device == dev and bias.dtype == torch.float32 and tuple(bias.shape) == (rows,)
               and bias.is_contiguous(), "bias must be a contiguous float32 [rows] tensor")
-    ws = _workspace(dev, 1, rows, cols) if split_k else None
+    if workspace is not None:
+        _need(workspace.device == dev and workspace.dtype == torch.uint8 and workspace.is_contiguous(),
+              "workspace must be a contiguous uint8 tensor on the weights' device (new_workspace)")
+        ws = workspace if split_k else None
+    else:
+        ws = _workspace(dev, 1, rows, cols) if split_k else None
     with torch.cuda.device(dev):
         status = _lib.lib().w4a16_gemv_fused(
             _ptr(packed), _ptr(scale), _SCALE_DTYPES[scale.dtype], group, prologue, _ptr(src),
             _ptr(gamma), float(eps), rows, cols, _ptr(out), _OUT_DTYPES[out.dtype], _ptr(bias),
-            _ptr(ws), ws.numel() if ws is not None else 0, _stream(dev))
+            _ptr(ws), ws.numel() if ws is not None else 0, _lib.LAUNCH_PDL if pdl else 0,
+            _stream(dev))
     _lib.check(status, "w4a16_gemv_fused")
     return out
 
 
+_CHAIN_DOC = """
+    Chaining: pdl=True launches with programmatic dependent launch, so the kernel loads
+    its first weights while the previous kernel in the stream finishes; consecutive
+    chained calls must then use different split-K workspaces (pass two buffers from
+    new_workspace alternately); workspace=None uses the per-device default."""
+
+
+def gemv_staged(packed, scale, x, *, group=0, bias=None, out=None, out_dtype=torch.float32,
+                split_k=True, pdl=False, workspace=None):
+    """W @ x (+ bias) for one fp16 vector x [cols] staged in shared memory.
+
+    The decode-step GEMV without a prologue (out may alias bias: in-place residual)."""
+    cols = packed.shape[1] * 2
+    _check_vec(x, cols, packed.device)
+    _need(x.dim() == 1, "gemv_staged takes one activation vector")
+    return _fused(_lib.PROLOGUE_NONE, packed, scale, x, None, 0.0, group, bias, out, out_dtype,
+                  split_k, pdl, workspace)
+
+
 def gemv_rmsnorm(packed, scale, h, gamma, eps=1e-5, *, group=0, bias=None, out=None,
-                 out_dtype=torch.float32, split_k=True):
+                 out_dtype=torch.float32, split_k=True, pdl=False, workspace=None):
     """W @ fp16(h * rsqrt(mean(h^2) + eps) * gamma) (+ bias): RMSNorm fused into the GEMV.
 
     h, gamma: fp32 [cols] on the weights' device.  out may alias bias (in-place residual)."""
@@ -169,24 +204,29 @@ def gemv_rmsnorm(packed, scale, h, gamma, eps=1e-5, *, group=0, bias=None, out=N
         _need(isinstance(t, torch.Tensor) and t.device == packed.device and t.dtype == torch.float32
               and tuple(t.shape) == (cols,) and t.is_contiguous(), f"{name} must be fp32 [{cols}]")
     return _fused(_lib.PROLOGUE_RMSNORM, packed, scale, h, gamma, eps, group, bias, out, out_dtype,
-                  split_k)
+                  split_k, pdl, workspace)
 
 
 def gemv_swiglu(packed, scale, gate_up, *, group=0, bias=None, out=None, out_dtype=torch.float32,
-                split_k=True):
+                split_k=True, pdl=False, workspace=None):
     """W @ fp16(silu(gate) * up) (+ bias) with gate_up = [gate | up] fp16 [2 * cols]."""
     cols = packed.shape[1] * 2
     _need(isinstance(gate_up, torch.Tensor) and gate_up.device == packed.device
           and gate_up.dtype == torch.float16 and tuple(gate_up.shape) == (2 * cols,)
           and gate_up.is_contiguous(), f"gate_up must be fp16 [{2 * cols}]")
     return _fused(_lib.PROLOGUE_SWIGLU, packed, scale, gate_up, None, 0.0, group, bias, out, out_dtype,
-                  split_k)
+                  split_k, pdl, workspace)
+
+
+for _f in (gemv_staged, gemv_rmsnorm, gemv_swiglu):
+    _f.__doc__ += _CHAIN_DOC
 
 
 _ATTN_SCRATCH = {}
 
 
-def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, out=None, splits=None):
+def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, out=None, splits=None,
+                     pdl=False):
     """One decode token's attention with rotary and the KV-cache write in one launch.
 
     qkv fp16 [(heads + 2 kv_heads) * 64] (q | k | v); cos, sin fp32 [max_len, 64]
@@ -194,7 +234,8 @@ def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, o
     [kv_heads, max_len, 64] (this layer's).  Writes k_cache/v_cache at pos and returns
     out fp16 [heads * 64].  splits: CTAs per kv head over the positions (default one per
     32 positions).  The zeroed scratch is kept per device and shape; allocate it (one
-    eager call) before capturing the op in a CUDA graph."""
+    eager call) before capturing the op in a CUDA graph.  pdl: programmatic dependent
+    launch (see gemv_staged)."""
     dev = qkv.device
     D = 64
     max_len = k_cache.shape[1]
@@ -225,7 +266,8 @@ def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, o
     with torch.cuda.device(dev):
         status = L.w4a16_decode_attention(
             _ptr(qkv), _ptr(cos), _ptr(sin), _ptr(pos), _ptr(k_cache), _ptr(v_cache), _ptr(out),
-            _ptr(scratch), scratch.numel(), heads, kv_heads, D, max_len, splits, _stream(dev))
+            _ptr(scratch), scratch.numel(), heads, kv_heads, D, max_len, splits,
+            _lib.LAUNCH_PDL if pdl else 0, _stream(dev))
     _lib.check(status, "w4a16_decode_attention")
     return out
 
