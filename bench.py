@@ -227,26 +227,37 @@ def run_ours(args, rank, world, dev):
     L = _lib.lib()
     sptr = ctypes.c_void_p(stream.cuda_stream)
 
-    ws = torch.zeros(int(L.w4a16_gemv_workspace_bytes(1, ROWS, COLS)), dtype=torch.uint8, device=dev)
+    # one split-K workspace per weight copy: consecutive launches alternate copies, so
+    # with chained launches two overlapping kernels never share a workspace
+    wsz = int(L.w4a16_gemv_workspace_bytes(1, ROWS, COLS))
+    wss = [torch.zeros(wsz, dtype=torch.uint8, device=dev) for _ in range(2)]
 
-    def gemv_fn(packed, scale, out, group):
-        # the library's general C entry point (w4a16_gemv), with its workspace, as the
-        # Python op w4a16.w4a16_gemv_g128 calls it
-        args_ = (ctypes.c_void_p(packed.data_ptr()), _lib.PACK_INTERLEAVED,
-                 ctypes.c_void_p(scale.data_ptr()), _lib.DTYPE_F32, group,
-                 ctypes.c_void_p(x.data_ptr()), 1, packed.shape[0], packed.shape[1] * 2,
-                 ctypes.c_void_p(out.data_ptr()), _lib.DTYPE_F32, None,
-                 ctypes.c_void_p(ws.data_ptr()), ws.numel())
+    def gemv_fn(packed, scale, out, group, ws, chained=True):
+        """One GEMV launch through the library's C ABI.  chained: w4a16_gemv_fused without
+        a prologue and with W4A16_LAUNCH_PDL, so that each launch loads its first weights
+        while the previous one drains (the way a decode step chains its GEMVs); otherwise
+        the general entry w4a16_gemv, as the Python op w4a16.w4a16_gemv_g128 calls it."""
+        P = ctypes.c_void_p
+        rows, cols = packed.shape[0], packed.shape[1] * 2
+        if chained:
+            args_ = (P(packed.data_ptr()), P(scale.data_ptr()), _lib.DTYPE_F32, group, _lib.PROLOGUE_NONE,
+                     P(x.data_ptr()), None, 0.0, rows, cols, P(out.data_ptr()), _lib.DTYPE_F32, None,
+                     P(ws.data_ptr()), ws.numel(), _lib.LAUNCH_PDL)
+            entry = L.w4a16_gemv_fused
+        else:
+            args_ = (P(packed.data_ptr()), _lib.PACK_INTERLEAVED, P(scale.data_ptr()), _lib.DTYPE_F32,
+                     group, P(x.data_ptr()), 1, rows, cols, P(out.data_ptr()), _lib.DTYPE_F32, None,
+                     P(ws.data_ptr()), ws.numel())
+            entry = L.w4a16_gemv
 
         def f():
-            s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-            st = L.w4a16_gemv(*args_, s)
+            st = entry(*args_, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
             if st != 0:
                 raise RuntimeError(L.w4a16_last_error_string().decode())
         return f
 
-    def step(packed, scale):
-        f = gemv_fn(packed, scale, y, GROUP)
+    def step(packed, scale, ws):
+        f = gemv_fn(packed, scale, y, GROUP, ws)
         if world == 1:
             return f
 
@@ -255,7 +266,7 @@ def run_ours(args, rank, world, dev):
             torch.distributed.all_gather_into_tensor(gathered, y)
         return g_
 
-    steps_fns = [step(p, s) for p, s in copies]
+    steps_fns = [step(p, s, w) for (p, s), w in zip(copies, wss)]
     for _ in range(args.warmup):
         for f in steps_fns:
             f()
@@ -286,7 +297,7 @@ def run_ours(args, rank, world, dev):
     if world == 1:
         kernel_us = step_us
     else:  # kernel alone, timed the same way
-        kf = [gemv_fn(p, s, y, GROUP) for p, s in copies]
+        kf = [gemv_fn(p, s, y, GROUP, w) for (p, s), w in zip(copies, wss)]
         kg, kc = build_step_graphs(kf, min(args.steps, 2000))
         kernel_us = time_graphs(kg, kc, min(args.steps, 2000), stream) * 1000.0 / min(args.steps, 2000)
         del kg
@@ -301,16 +312,27 @@ def run_ours(args, rank, world, dev):
     if rank == 0:
         # per-row variant of the same shape
         prow = [make_weights(ROWS, COLS, 0, seed=50 + c, device=dev) for c in range(2)]
-        rf = [gemv_fn(p, s, y, 0) for p, s in prow]
         n = min(args.steps, 2000)
-        rg, rc = build_step_graphs(rf, n)
-        rg[0].replay()
-        row_us = time_graphs(rg, rc, n, stream) * 1000.0 / n
-        del rg
+
+        def timed(fns):
+            gs, cs = build_step_graphs(fns, n)
+            gs[0].replay()
+            us = time_graphs(gs, cs, n, stream) * 1000.0 / n
+            del gs
+            return us
+
+        row_us = timed([gemv_fn(p, s, y, 0, w) for (p, s), w in zip(prow, wss)])
+        row_plain_us = timed([gemv_fn(p, s, y, 0, w, chained=False) for (p, s), w in zip(prow, wss)])
+        g128_plain_us = timed([gemv_fn(p, s, y, GROUP, w, chained=False) for (p, s), w in zip(copies, wss)])
         rbytes = algorithmic_bytes(ROWS, COLS, 0)
         extras["per_row_us"] = round(row_us, 3)
         extras["per_row_frac_of_peak"] = round(rbytes / (row_us * 1e-6) / 1e9 / peak, 4)
         extras["g128_frac_of_peak"] = result["roofline"]["frac"]
+        # the same launches without chaining (each kernel starts after the previous ends)
+        extras["g128_unchained_us"] = round(g128_plain_us, 3)
+        extras["g128_unchained_frac_of_peak"] = round(nbytes / (g128_plain_us * 1e-6) / 1e9 / peak, 4)
+        extras["per_row_unchained_us"] = round(row_plain_us, 3)
+        extras["per_row_unchained_frac_of_peak"] = round(rbytes / (row_plain_us * 1e-6) / 1e9 / peak, 4)
         # cuBLAS fp16 F.linear on the same shape (dense weights, 1 GiB per copy)
         dense = [torch.randn(ROWS, COLS, device=dev, dtype=torch.float16) * 0.02 for _ in range(2)]
         xb = x.view(1, COLS)
@@ -327,6 +349,7 @@ def run_ours(args, rank, world, dev):
         extras["cublas_fp16_linear_us"] = round(cublas_us, 3)
         extras["speedup_vs_cublas_g128"] = round(cublas_us / kernel_us, 3)
         extras["speedup_vs_cublas_per_row"] = round(cublas_us / row_us, 3)
+        extras["speedup_vs_cublas_g128_unchained"] = round(cublas_us / g128_plain_us, 3)
         del prow
         torch.cuda.empty_cache()
 
@@ -523,7 +546,10 @@ def main():
                    "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
                    "value_definition": "device time per 262144x2048 GEMV-equivalent (step time / GEMVs per step)",
                    "l2": "inputs larger than L2: 2 rotating copies of 285 MB packed weights+scales",
-                   "timing": "CUDA events around CUDA-graph replays of K launches of the C entry w4a16_gemv"},
+                   "timing": "CUDA events around CUDA-graph replays of K back-to-back launches of the C "
+                             "entry w4a16_gemv_fused (no prologue) chained with programmatic dependent "
+                             "launch: each GEMV reads all its weights, its start overlaps the previous "
+                             "one's drain; extras give the unchained w4a16_gemv figures"},
         "roofline": res["roofline"],
         "cpu_baseline": res.get("cpu_baseline"),
         "e2e": res["e2e"],

@@ -138,7 +138,7 @@ int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_
  *   W4A16_PROLOGUE_SWIGLU   src = fp16 [2*cols] = gate | up:  x = fp16(silu(gate) * up)
  * One activation vector; interleaved packing; cols % 256 == 0 and small enough for the
  * vector to sit in shared memory beside the weight rings (cols <= 10752 with group-128
- * fp32 scales, <= 16896 with one scale per row).  out (fp32 or fp16 [rows]) may alias
+ * fp32 scales, <= 16640 with one scale per row).  out (fp32 or fp16 [rows]) may alias
  * bias (fp32): out = W x + bias is then an in-place residual add.  out must not overlap
  * src.  flags: 0 or W4A16_LAUNCH_PDL. */
 int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, int group,

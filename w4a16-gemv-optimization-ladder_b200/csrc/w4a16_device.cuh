@@ -28,6 +28,7 @@ constexpr uint32_t kHiMask = 0x00f000f0u;    // nibble 1 of each 16-bit half
 constexpr uint32_t k1032x2 = 0x64086408u;    // {1032, 1032}
 constexpr uint32_t kSixteenth = 0x2c002c00u; // {1/16, 1/16}
 constexpr uint32_t kMinus72x2 = 0xd480d480u; // {-72, -72}
+constexpr uint32_t kExp64x2 = 0x54005400u;   // {64, 64}
 // LUT operand of lop3 for (a & b) | c, built from the canonical inputs
 // a = 0xF0, b = 0xCC, c = 0xAA.
 constexpr uint32_t kLutAndOr = (0xF0 & 0xCC) | 0xAA;
@@ -81,6 +82,19 @@ __device__ __forceinline__ void decode_word(uint32_t w, uint32_t (&o)[4]) {
   o[3] = fma_f16x2(hi1, kSixteenth, kMinus72x2);
 }
 
+// The same four f16x2 with nibble 1 of each byte pair left biased: o[1] and o[3]
+// hold 64 + n = q + 72 exactly (nibble at mantissa bits 4-7 under exponent 64), so no
+// f16x2 operation is spent on them.  Seven instructions: one shift, four lop3, two
+// f16x2 subtractions.  The caller removes 72 * (sum of the activation over those
+// columns: pairs (2,3) and (6,7) of every 8 for the interleaved packing) per group.
+__device__ __forceinline__ void decode_word_fold(uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t w8 = w >> 8;
+  o[0] = sub_f16x2(lop3_and_or(w, kLoMask, kExp16x2), k1032x2);
+  o[1] = lop3_and_or(w, kHiMask, kExp64x2);
+  o[2] = sub_f16x2(lop3_and_or(w8, kLoMask, kExp16x2), k1032x2);
+  o[3] = lop3_and_or(w8, kHiMask, kExp64x2);
+}
+
 // Reorder an 8-column activation chunk (four f16x2: (x0,x1) (x2,x3) (x4,x5) (x6,x7))
 // into the column pairs that decode_word produces for the simple packing:
 // (x1,x5) (x0,x4) (x3,x7) (x2,x6).
@@ -100,6 +114,15 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A * B + c (every element of C = c): starts an accumulation at an offset.
+__device__ __forceinline__ void mma_16816_c(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1, float c) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c));
 }
 
 // D = A * B (C = 0): starts a fresh accumulation without zeroed registers.

@@ -36,6 +36,12 @@
 #include "w4a16_device.cuh"
 #include "w4a16_internal.h"
 
+#ifndef W4A16_L2_PROMOTION  // L2 fill granularity of the weight copies (CU_TENSOR_MAP_L2_PROMOTION_*)
+#define W4A16_L2_PROMOTION 2  // 128 bytes (64, 128 and 256 measured within 0.2%)
+#endif
+#ifndef W4A16_FOLD  // batch-1 decode with half the nibbles left biased (decode_word_fold)
+#define W4A16_FOLD 1
+#endif
 #ifndef W4A16_TMA_WARPS
 #define W4A16_TMA_WARPS 12
 #endif
@@ -207,20 +213,31 @@ __device__ __forceinline__ LaneOffsets lane_offsets(int g, int t) {
   return o;
 }
 
-template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS>
+// FOLD (one activation vector, interleaved packing): weights decoded with
+// decode_word_fold; every 128-column group starts its accumulator at corr[group] =
+// -72 * (sum of x over the group's biased columns), which cancels the bias exactly up
+// to fp32 rounding, and is then added (scaled, for group-128) into tot.
+template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS, bool FOLD>
 __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, uint32_t xs,
-                                               int nslab, int kcol0, const TmaParams& p, int g,
-                                               int t, const LaneOffsets& lo,
+                                               uint32_t corr, int nslab, int kcol0,
+                                               const TmaParams& p, int g, int t,
+                                               const LaneOffsets& lo,
                                                float (&acc)[RT][2][BatchCfg<NB>::kHalves][4],
                                                float (&tot)[RT][BatchCfg<NB>::kHalves][4]) {
   // activation fragments of this window: 16 bytes at xwin + ((sl*2 + gh)*4 + j)*64
   const uint32_t xwin = xs + lo.x + (uint32_t)(kcol0 >> 7) * 256u;
   constexpr int NH = BatchCfg<NB>::kHalves;
   constexpr int kGroups = SLABS * 2;
+  static_assert(!FOLD || (NB == 1 && PACK == W4A16_PACK_INTERLEAVED), "FOLD: one vector, interleaved");
 #pragma unroll
   for (int sl = 0; sl < SLABS; ++sl) {
     if (FULL || sl < nslab) {
       const int kcol = kcol0 + sl * kSlabCols;
+      float cinit[2] = {0.f, 0.f};
+      if (FOLD) {
+#pragma unroll
+        for (int gh = 0; gh < 2; ++gh) cinit[gh] = lds_f32(corr + (uint32_t)((kcol >> 7) + gh) * 4u);
+      }
       uint4 wa[RT][2], wb[RT][2];
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
@@ -250,11 +267,18 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
             const uint32_t word_a = j == 0 ? va.x : j == 1 ? va.y : j == 2 ? va.z : va.w;
             const uint32_t word_b = j == 0 ? vb.x : j == 1 ? vb.y : j == 2 ? vb.z : vb.w;
             uint32_t A[4], B[4];
-            decode_word(word_a, A);
-            decode_word(word_b, B);
+            if (FOLD) {
+              decode_word_fold(word_a, A);
+              decode_word_fold(word_b, B);
+            } else {
+              decode_word(word_a, A);
+              decode_word(word_b, B);
+            }
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
-              if (GS && j == 0)
+              if (FOLD && j == 0)
+                mma_16816_c(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y, cinit[gh]);
+              else if (GS && j == 0)
                 mma_16816_zc(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
               else
                 mma_16816(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
@@ -286,6 +310,15 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
               tot[rt][h][3] = fmaf(s1, acc[rt][gh][h][3], tot[rt][h][3]);
             }
           }
+      } else if (FOLD) {  // per-row scale: the groups are summed unscaled
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+          for (int gh = 0; gh < 2; ++gh)
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) tot[rt][h][i] += acc[rt][gh][h][i];
       }
     }
   }
@@ -318,8 +351,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // fragment is then one shared-memory load.  The staging comes after the first
   // weight copies are in flight.
   constexpr bool XS = XM != kXGlobal;
+  constexpr bool FOLD = W4A16_FOLD && NB == 1 && PACK == W4A16_PACK_INTERLEAVED;
   using Plan = SmemPlan<WARPS, STAGES, L>;
+  // after the rings: [staged x: 2K bytes if XS][128-byte scratch][FOLD corrections:
+  // K/128 floats, 128-byte padded][kSchedLocal partial sums]
   const uint32_t xs = base + (uint32_t)Plan::kXOff;
+  const uint32_t red_off = XS ? (uint32_t)p.K * 2u : 0u;
+  const uint32_t corr = xs + red_off + 128u;
+  const uint32_t corr_bytes = FOLD ? (uint32_t)(((p.K >> 7) * 4 + 127) & ~127) : 0u;
 
   const bool local = p.sched == kSchedLocal;
   const int ks = p.kslabs;
@@ -416,19 +455,39 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   // kSchedLocal partial sums [unit of the CTA][16 rows] sit after the staged vector;
   // slots no segment starts at stay zero
-  float* lpart = reinterpret_cast<float*>(smem_raw + (xs - smem_addr(smem_raw)) +
-                                          (XS ? (size_t)p.K * 2 + 128 : 0));
+  float* lpart = reinterpret_cast<float*>(smem_raw + (corr - smem_addr(smem_raw)) + corr_bytes);
   if (local) {
     for (int i = threadIdx.x; i < LocalPlan<WARPS, STAGES, kRows>::kUnits * kRows; i += blockDim.x)
       lpart[i] = 0.f;
     if (!XS) __syncthreads();
   }
 
+  // FOLD: corr[g] = -72 * (sum of the fp16 activation over columns 8i+2, 8i+3, 8i+6,
+  // 8i+7 of group g), summed by the 16 threads holding the group's 16 chunks (a
+  // thread's chunks are warp-uniformly in or out of range: K is a multiple of 256).
+  const int nch = p.K >> 3;  // 8-element chunks; thread i takes chunks i, i + blockDim, ...
+  float* corr_f = reinterpret_cast<float*>(smem_raw + (corr - smem_addr(smem_raw)));
+  auto fold_correction = [&](int c, const uint4& v) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+    float part = (a.x + a.y) + (b.x + b.y);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if ((lane & 15) == 0 && c < nch) corr_f[c >> 4] = -72.f * part;
+  };
+  if (FOLD && !XS) {  // the vector stays in global memory: read it once for the sums
+    for (int c0 = 0; c0 < nch; c0 += blockDim.x) {
+      const int c = c0 + threadIdx.x;
+      const uint4 v = c < nch ? ldcg128(p.x + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+      fold_correction(c, v);
+    }
+    __syncthreads();
+  }
+
   if (XS) {
     // x, h, gate|up and the bias may have been written by the previous kernel:
     // read them through L2 (ldcg), not the non-coherent path.
     uint8_t* xsp = smem_raw + (xs - smem_addr(smem_raw));
-    const int nch = p.K >> 3;  // 8-element chunks; thread i takes chunks i, i + blockDim, ...
     // Every loop below is unrolled over kStageChunks chunks per thread with a guard, so a
     // thread's loads are all in flight together (the host stages only K <= kStageChunks *
     // threads * 8).
@@ -436,7 +495,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll
       for (int j = 0; j < kStageChunks; ++j) {
         const int c = threadIdx.x + j * WARPS * 32;
-        if (c < nch) *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = ldcg128(p.x + c * 8);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (c < nch) {
+          v = ldcg128(p.x + c * 8);
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = v;
+        }
+        if (FOLD) fold_correction(c, v);
       }
     } else if (XM == kXRmsNorm) {
       const float4* h4 = static_cast<const float4*>(p.pro_src);
@@ -459,7 +523,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      float* red = reinterpret_cast<float*>(xsp + (size_t)p.K * 2);  // WARPS partial sums
+      float* red = reinterpret_cast<float*>(xsp + red_off);  // WARPS partial sums
       if (lane == 0) red[warp] = ss;
       __syncthreads();
       float tot = 0.f;
@@ -469,21 +533,24 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 #pragma unroll
       for (int j = 0; j < kStageChunks; ++j) {
         const int c = threadIdx.x + j * WARPS * 32;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (c < nch) {
           const float4 a = __ldcg(h4 + 2 * c), b = __ldcg(h4 + 2 * c + 1);
           const float4 ga = __ldg(g4 + 2 * c), gb = __ldg(g4 + 2 * c + 1);
-          const uint32_t p0 = pack_half2(a.x * r * ga.x, a.y * r * ga.y);
-          const uint32_t p1 = pack_half2(a.z * r * ga.z, a.w * r * ga.w);
-          const uint32_t p2 = pack_half2(b.x * r * gb.x, b.y * r * gb.y);
-          const uint32_t p3 = pack_half2(b.z * r * gb.z, b.w * r * gb.w);
-          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(p0, p1, p2, p3);
+          v.x = pack_half2(a.x * r * ga.x, a.y * r * ga.y);
+          v.y = pack_half2(a.z * r * ga.z, a.w * r * ga.w);
+          v.z = pack_half2(b.x * r * gb.x, b.y * r * gb.y);
+          v.w = pack_half2(b.z * r * gb.z, b.w * r * gb.w);
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = v;
         }
+        if (FOLD) fold_correction(c, v);
       }
     } else if (XM == kXSwiGlu) {
       const __half* gu = static_cast<const __half*>(p.pro_src);
 #pragma unroll
       for (int j = 0; j < kStageChunks; ++j) {
         const int c = threadIdx.x + j * WARPS * 32;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (c < nch) {
           const uint4 gv = ldcg128(gu + c * 8);
           const uint4 uv = ldcg128(gu + p.K + c * 8);
@@ -496,8 +563,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uw4[i]));
             pk[i] = pack_half2(g2.x / (1.0f + expf(-g2.x)) * u2.x, g2.y / (1.0f + expf(-g2.y)) * u2.y);
           }
-          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = v;
         }
+        if (FOLD) fold_correction(c, v);
       }
     }
     __syncthreads();
@@ -554,10 +623,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int s0 = win * SLABS;
     const int nslab = min(SLABS, ks - s0);
     if (nslab == SLABS)
-      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS>(wbase, sbase, xs, nslab, s0 * kSlabCols,
+      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS, FOLD>(wbase, sbase, xs, corr, nslab, s0 * kSlabCols,
                                                             p, g, t, lo, acc, tot);
     else
-      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS>(wbase, sbase, xs, nslab, s0 * kSlabCols,
+      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS, FOLD>(wbase, sbase, xs, corr, nslab, s0 * kSlabCols,
                                                              p, g, t, lo, acc, tot);
     __syncwarp();  // every lane has read the slot before it is refilled
     issue_one();
@@ -571,7 +640,17 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (!tile_done && (dyn || consumed + 1 < count)) continue;  // the tile goes on here
 
     // ---- tile epilogue
-    if (!GS) {
+    if (!GS && FOLD) {  // the groups were summed into tot: apply the row scale
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          tot[rt][h][0] *= srow[rt][0];
+          tot[rt][h][1] *= srow[rt][0];
+          tot[rt][h][2] *= srow[rt][1];
+          tot[rt][h][3] *= srow[rt][1];
+        }
+    } else if (!GS) {
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -842,11 +921,20 @@ constexpr int tma_smem_bytes() {
   return SmemPlan<kWarps, kStages, L>::kBytes;
 }
 
+// Shared memory after the weight/scale rings (the kernel's layout): the staged vector,
+// a 128-byte scratch, the FOLD corrections; kSchedLocal adds its partial sums.
+template <int PACK, int NB, int XM>
+int tail_smem_bytes(int K) {
+  constexpr bool fold = W4A16_FOLD && NB == 1 && PACK == W4A16_PACK_INTERLEAVED;
+  const int corr = fold ? ((K / 128) * 4 + 127) / 128 * 128 : 0;
+  return (XM != kXGlobal ? K * 2 : 0) + (NB == 1 ? 128 : 0) + corr;
+}
+
 template <int PACK, int GS, typename ST, int NB, typename OT, int XM>
 int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
   using L = StageLayout<kSlabs, kRT, GS, ST>;
   auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM>;
-  const int smem_base = tma_smem_bytes<GS, ST>() + (XM != kXGlobal ? p.K * 2 + 128 : 0);
+  const int smem_base = tma_smem_bytes<GS, ST>() + tail_smem_bytes<PACK, NB, XM>(p.K);
   int smem = smem_base;
   if (smem > di.smem_optin) {
     set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
@@ -878,7 +966,7 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
     const cuuint32_t estr[3] = {1, 1, 1};
     r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(p.packed), dims, strides,
             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            (CUtensorMapL2promotion)W4A16_L2_PROMOTION, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled(weights) failed: %d", (int)r);
       return W4A16_ERR_CUDA;
@@ -991,12 +1079,14 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
     return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
   } else {
   if (!use_tma) return launch_generic<PACK, GS, ST, OT>(p, x, M, y);
-  const bool xs_fits = tma_smem_bytes<GS, ST>() + p.K * 2 + 128 <= di.smem_optin &&
+  const bool xs_fits = tma_smem_bytes<GS, ST>() + tail_smem_bytes<PACK, 1, kXCopy>(p.K) <= di.smem_optin &&
                        p.K <= kStageChunks * 8 * kWarps * 32;
   if (p.staged) {
     if (M != 1 || !xs_fits) {
-      set_error("the staged (fused) GEMV needs one activation vector and cols <= %d",
-                (di.smem_optin - tma_smem_bytes<GS, ST>() - 128) / 2);
+      int kmax = kStageChunks * 8 * kWarps * 32;
+      while (kmax > 0 && tma_smem_bytes<GS, ST>() + tail_smem_bytes<PACK, 1, kXCopy>(kmax) > di.smem_optin)
+        kmax -= 256;
+      set_error("the staged (fused) GEMV needs one activation vector and cols <= %d", kmax);
       return W4A16_ERR_SHAPE;
     }
     if constexpr (PACK == W4A16_PACK_INTERLEAVED) {
