@@ -9,10 +9,12 @@ steps, so every step streams its weights from HBM.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 (launched by torchrun, one rank per GPU, NCCL): every rank holds its own
-262144-row shard of an (N*262144) x 2048 matrix (weak scaling), runs the GEMV and
-all-gathers the outputs; value = device step time (max over ranks) / N, i.e. µs
-per 262144x2048 GEMV-equivalent of the whole job.
+N > 1 (launched by torchrun, one rank per GPU): every rank holds its own 262144-row
+shard of an (N*262144) x 2048 matrix (weak scaling) and assembles the full output on
+every rank, timed two ways: the GEMV with the all-gather fused into its epilogue (each
+output row stored into every rank's gathered buffer over NVLink; w4a16_gemv_allgather)
+and the GEMV followed by an NCCL all-gather; value = the faster device step time (max
+over ranks) / N, i.e. µs per 262144x2048 GEMV-equivalent of the whole job.
 
 --impl reference times the reference's CPU path (fp32 dequant then matmul,
 src/w4a16/kernels.py:98-101) as restated by the C oracle, on all host threads.
@@ -223,7 +225,12 @@ def run_ours(args, rank, world, dev):
     g = torch.Generator(device=dev).manual_seed(7)
     x = torch.randn(COLS, device=dev, generator=g).half()
     y = torch.empty(ROWS, dtype=torch.float32, device=dev)
-    gathered = torch.empty(world * ROWS, dtype=torch.float32, device=dev) if world > 1 else None
+    tpa = None
+    if world > 1:
+        # rank r owns rows [r*ROWS, (r+1)*ROWS) of the (world*ROWS) x COLS matrix; its GEMV's
+        # epilogue writes them into every rank's gathered output over NVLink
+        from w4a16.tp import FusedAllGatherW4A16
+        tpa = FusedAllGatherW4A16(copies[0][0], copies[0][1], world * ROWS, group=GROUP)
     L = _lib.lib()
     sptr = ctypes.c_void_p(stream.cuda_stream)
 
@@ -257,33 +264,58 @@ def run_ours(args, rank, world, dev):
         return f
 
     def step(packed, scale, ws):
-        f = gemv_fn(packed, scale, y, GROUP, ws)
         if world == 1:
-            return f
+            return gemv_fn(packed, scale, y, GROUP, ws)
 
-        def g_():
-            f()
-            torch.distributed.all_gather_into_tensor(gathered, y)
+        def g_():  # w4a16_gemv_allgather: the GEMV with the all-gather fused, chained launches
+            tpa.launch(packed, scale, x, stream=ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                       pdl=True)
         return g_
 
     steps_fns = [step(p, s, w) for (p, s), w in zip(copies, wss)]
-    for _ in range(args.warmup):
-        for f in steps_fns:
-            f()
-    torch.cuda.synchronize()
-    graphs, counts = build_step_graphs(steps_fns, args.steps)
-    graphs[0].replay()  # warm the graph
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+
+    def measure(fns, sampler=None):
+        """Warm-up, then K steps from CUDA graphs; device ms, max over ranks."""
+        for _ in range(args.warmup):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        graphs, counts = build_step_graphs(fns, args.steps)
+        graphs[0].replay()  # warm the graph
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        ms_ = time_graphs(graphs, counts, args.steps, stream, sampler)
+        if world > 1:
+            t = torch.tensor([ms_], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms_ = t.item()
+            torch.distributed.barrier()
+        del graphs  # graphs holding NCCL calls go before the process group does
+        torch.cuda.synchronize()
+        return ms_
+
     sampler = ClockSampler(dev.index) if rank == 0 else None
-    ms = time_graphs(graphs, counts, args.steps, stream, sampler)
+    ms = measure(steps_fns, sampler)
+    tp_choice = None
     if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = t.item()
-        torch.distributed.barrier()
-    del graphs
+        # the same steps with the GEMV followed by an NCCL all-gather; the faster of the
+        # two strategies is the reported value, both are in the extras
+        gathered = torch.empty(world * ROWS, dtype=torch.float32, device=dev)
+
+        def nccl_step(packed, scale, ws):
+            f = gemv_fn(packed, scale, y, GROUP, ws)
+
+            def g_():
+                f()
+                torch.distributed.all_gather_into_tensor(gathered, y)
+            return g_
+
+        ms_nccl = measure([nccl_step(p, s, w) for (p, s), w in zip(copies, wss)])
+        tp_choice = {"fused_step_us": round(ms * 1000.0 / args.steps, 3),
+                     "nccl_step_us": round(ms_nccl * 1000.0 / args.steps, 3)}
+        tp_choice["chosen"] = "fused" if ms <= ms_nccl else "nccl"
+        ms = min(ms, ms_nccl)
     step_us = ms * 1000.0 / args.steps
     if rank == 0:
         print(f"[bench] g128 262144x2048: {step_us:.3f} us/step over {args.steps} steps",
@@ -309,6 +341,8 @@ def run_ours(args, rank, world, dev):
                           "kernel_us": round(kernel_us, 3)}
 
     extras = {}
+    if tp_choice is not None:
+        extras["tensor_parallel"] = tp_choice
     if rank == 0:
         # per-row variant of the same shape
         prow = [make_weights(ROWS, COLS, 0, seed=50 + c, device=dev) for c in range(2)]
@@ -360,7 +394,7 @@ def run_ours(args, rank, world, dev):
     packed_h = copies[0][0].cpu().pin_memory()
     scale_h = copies[0][1].cpu().pin_memory()
     x_h = x.cpu().pin_memory()
-    y_h = torch.empty(ROWS, dtype=torch.float32).pin_memory()
+    y_h = torch.empty(world * ROWS, dtype=torch.float32).pin_memory()
     pd = torch.empty_like(copies[0][0])
     sd = torch.empty_like(copies[0][1])
     xd = torch.empty_like(x)
@@ -370,9 +404,10 @@ def run_ours(args, rank, world, dev):
         pd.copy_(packed_h, non_blocking=True)
         sd.copy_(scale_h, non_blocking=True)
         xd.copy_(x_h, non_blocking=True)
-        out = K.w4a16_gemv_g128(pd, sd, xd)
-        if world > 1:
-            torch.distributed.all_gather_into_tensor(gathered, out)
+        if world > 1:  # the full gathered output comes back to the host on every rank
+            out = tpa.launch(pd, sd, xd)
+        else:
+            out = K.w4a16_gemv_g128(pd, sd, xd)
         y_h.copy_(out, non_blocking=True)
         return out
 
@@ -394,7 +429,9 @@ def run_ours(args, rank, world, dev):
     result["e2e"] = {"value": round(e2e_ms * 1000.0 / e2e_steps / world, 3), "unit": "µs",
                      "h2d_bytes_per_step": packed_h.numel() + scale_h.numel() * 4 + x_h.numel() * 2,
                      "d2h_bytes_per_step": y_h.numel() * 4,
-                     "steps": e2e_steps, "api": "w4a16.w4a16_gemv_g128 (C ABI w4a16_gemv)"}
+                     "steps": e2e_steps,
+                     "api": ("w4a16.tp.FusedAllGatherW4A16 (C ABI w4a16_gemv_allgather)" if world > 1
+                             else "w4a16.w4a16_gemv_g128 (C ABI w4a16_gemv)")}
 
     # correctness of the benchmarked kernel on this data, against the oracle (rank 0)
     if rank == 0:
@@ -414,6 +451,8 @@ def run_ours(args, rank, world, dev):
                                                 "(C oracle: fp32 dequant then fp32 dot, pthreads)"}
     result["clocks"] = sampler.summary() if sampler else None
     result["extras"] = extras
+    if tpa is not None:
+        tpa.close()
     return result
 
 
@@ -543,7 +582,10 @@ def main():
         "data": "synthetic (seeded N(0,0.02) fp16 weights quantised g128, N(0,1) fp16 x)",
         "config": {"workload": "g128 int4 GEMV 262144x2048, batch 1",
                    "rows_per_gpu": ROWS, "cols": COLS, "group": GROUP,
-                   "parallelism": f"row-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "parallelism": (f"row-shard x{world}; all-gather fused into the GEMV epilogue "
+                                   "(NVLink peer stores) or GEMV + NCCL all-gather, whichever was "
+                                   "faster in this run (extras.tensor_parallel)") if world > 1
+                                  else "single GPU",
                    "value_definition": "device time per 262144x2048 GEMV-equivalent (step time / GEMVs per step)",
                    "l2": "inputs larger than L2: 2 rotating copies of 285 MB packed weights+scales",
                    "timing": "CUDA events around CUDA-graph replays of K back-to-back launches of the C "

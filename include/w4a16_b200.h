@@ -168,6 +168,37 @@ int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin
 
 size_t w4a16_decode_attention_scratch_bytes(int heads, int kv_heads, int splits);
 
+/* Tensor parallel with the all-gather fused into the GEMV (no counterpart in the
+ * reference, which has one GPU; the unfused form is the local GEMV followed by
+ * ncclAllGather).  Every rank owns one region of w4a16_tp_header_bytes() + the gathered
+ * output's bytes, allocated by w4a16_tp_region_alloc on its GPU (zero-filled), and opens
+ * the other ranks' regions from their IPC handles (w4a16_tp_region_open; handle size
+ * w4a16_tp_ipc_handle_bytes()).  All ranks start from freshly allocated regions and make
+ * the same sequence of calls on their streams. */
+size_t w4a16_tp_header_bytes(void);
+size_t w4a16_tp_ipc_handle_bytes(void);
+int w4a16_tp_region_alloc(size_t out_bytes, void** region, void* ipc_handle);
+int w4a16_tp_region_open(const void* ipc_handle, void** region);
+int w4a16_tp_region_close(void* region, int owned);
+
+/* One step, one kernel: this rank's rows [row0, row0 + rows) of y = W x (interleaved
+ * packing, one fp16 vector x [cols], out_dtype fp32 or fp16) are written by the GEMV's
+ * epilogue straight into the gathered output of every rank (regions[k] +
+ * w4a16_tp_header_bytes(), NVLink stores to the peers).  Each rank announces the step when
+ * its kernel starts; a warp stores into other ranks' buffers only once every rank has
+ * announced it (so no rank overwrites a buffer a peer is still reading from the previous
+ * step); the kernel's last CTA publishes this rank's completion and waits for every rank's,
+ * so when the call completes on the stream the gathered output is whole on this rank.
+ * Waits are bounded (2 s): a missing peer sets the device error word
+ * (w4a16_read_device_error, code 2) and the step then writes this rank's own rows only.
+ * regions: host array of nranks device pointers (own region at index rank).  Stream-ordered
+ * and graph-capturable: step numbers live in the regions.  flags: 0 or W4A16_LAUNCH_PDL
+ * (then consecutive calls must alternate two workspaces, as for w4a16_gemv_fused). */
+int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dtype, int group,
+                         const void* x, int rows, int cols, int out_dtype, long long row0, int rank,
+                         int nranks, void* const* regions, void* workspace, size_t workspace_bytes,
+                         unsigned flags, w4a16_stream_t stream);
+
 /* Bytes of workspace that let w4a16_gemv balance its work across warps (stream-K)
  * for this batch size; independent of rows and cols (about 0.5 MiB per activation
  * row, at most 16 of them per pass). */

@@ -148,3 +148,28 @@ def test_decode_attention_host_validation(lib):
     assert _attn(lib, scratch_bytes=100) == -5
     assert b"scratch" in lib.w4a16_last_error_string()
     assert _attn(lib, flags=4) == -4
+
+
+def test_tensor_parallel_host_validation(lib):
+    assert lib.w4a16_tp_header_bytes() == 256
+    assert lib.w4a16_tp_ipc_handle_bytes() == 64
+    p = ctypes.c_void_p
+    assert lib.w4a16_tp_region_alloc(1024, None, None) == -1
+    assert lib.w4a16_tp_region_open(None, None) == -1
+    assert lib.w4a16_tp_region_close(None, 1) == 0
+
+    def call(regions=((1 << 20), (2 << 20)), rank=0, nranks=2, rows=16, row0=0, cols=256, flags=0):
+        arr = (ctypes.c_void_p * len(regions))(*regions) if regions is not None else None
+        return lib.w4a16_gemv_allgather(p(1 << 12), p(1 << 12), 0, 0, p(1 << 16), rows, cols, 0, row0,
+                                        rank, nranks, arr, None, 0, flags, None)
+
+    assert call(regions=None) == -1
+    assert call(nranks=1) == -2
+    assert call(nranks=9) == -2
+    assert call(rank=2) == -2
+    assert call(rows=0) == -2
+    assert call(row0=-16) == -2
+    assert call(regions=((1 << 20), (2 << 20) + 64)) == -3   # regions 256-byte aligned
+    assert call(regions=((1 << 20), 0)) == -1
+    assert call(cols=200) == -2
+    assert call(flags=2) == -4

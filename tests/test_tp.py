@@ -3,6 +3,7 @@
 The local product is the oracle (numpy) here, so the test covers the sharding,
 padding and all-gather reassembly; the GPU path runs the same wrapper with the
 library GEMV and NCCL (tests/test_gpu_tp.py)."""
+import ctypes
 import os
 import socket
 
@@ -76,3 +77,82 @@ def test_row_sharded_gather_matches_full_product(world, rows, cols, group, batch
     for rank, err, shape in results:
         assert shape == want_shape
         assert err < 1e-5, f"rank {rank}: max err {err}"
+
+
+class _FakeTpLib:
+    """Stands in for the library's region / IPC / launch calls on CPU ranks."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened, self.closed, self.launches = [], [], []
+
+    def w4a16_tp_ipc_handle_bytes(self):
+        return 64
+
+    def w4a16_tp_header_bytes(self):
+        return 256
+
+    def w4a16_tp_region_alloc(self, nbytes, pptr, handle):
+        pptr._obj.value = (self.rank + 1) << 20
+        tag = f"region-of-rank-{self.rank}-{nbytes}".encode()
+        ctypes.memmove(handle, tag.ljust(64, b"\0"), 64)
+        return 0
+
+    def w4a16_tp_region_open(self, handle, pptr):
+        text = handle.raw.rstrip(b"\0").decode()
+        self.opened.append(text)
+        pptr._obj.value = (int(text.split("-")[3]) + 1) << 20
+        return 0
+
+    def w4a16_tp_region_close(self, ptr, owned):
+        self.closed.append((ptr.value, owned))
+        return 0
+
+    def w4a16_gemv_allgather(self, packed, scale, sdt, group, x, rows, cols, odt, row0, rank, nranks,
+                             regions, ws, wsb, flags, stream):
+        self.launches.append((rows, cols, row0, rank, nranks, [regions[k] for k in range(nranks)]))
+        return 0
+
+
+def _fused_host_worker(rank, world, port, rows, q):
+    from w4a16.tp import FusedAllGatherW4A16
+
+    class CpuFused(FusedAllGatherW4A16):
+        def _make_out(self, ptr, n, dtype):
+            self.out_ptr = ptr
+            return torch.zeros(n, dtype=dtype)
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lib = _FakeTpLib(rank)
+        lo, hi = shard_bounds(rows, world, rank)
+        packed = torch.zeros(hi - lo, 128, dtype=torch.uint8)
+        scale = torch.ones(hi - lo, 2)
+        tp = CpuFused(packed, scale, rows, group=128, lib=lib)
+        tp.launch(packed, scale, torch.zeros(256, dtype=torch.float16), stream=ctypes.c_void_p(0))
+        tp.close()
+        q.put((rank, tp.regions, lib.opened, lib.launches, lib.closed, tp.out_ptr, (lo, hi)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,rows", [(2, 1000), (3, 4096)])
+def test_fused_allgather_host_logic(world, rows):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_host_worker, args=(r, world, port, rows, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = [(k + 1) << 20 for k in range(world)]
+    for rank, regions, opened, launches, closed, out_ptr, (lo, hi) in results:
+        assert regions == want                                  # every rank's region, in rank order
+        assert sorted(opened) == sorted(f"region-of-rank-{k}-{rows * 4}" for k in range(world) if k != rank)
+        assert launches == [(hi - lo, 256, lo, rank, world, want)]
+        assert out_ptr == want[rank] + 256                      # output after the header
+        assert sorted(closed) == sorted([(w, 0) for k, w in enumerate(want) if k != rank] + [(want[rank], 1)])

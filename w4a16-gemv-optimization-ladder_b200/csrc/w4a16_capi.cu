@@ -3,6 +3,7 @@
 // shape, alignment or dtype code returns a status and launches nothing.
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "w4a16_b200.h"
 #include "w4a16_internal.h"
@@ -269,6 +270,115 @@ int w4a16_decode_attention(const void* qkv, const float* cos_t, const float* sin
 size_t w4a16_decode_attention_scratch_bytes(int heads, int kv_heads, int splits) {
   if (heads <= 0 || kv_heads <= 0 || splits <= 0) return 0;
   return w4a16::decode_attention_scratch_bytes(heads, kv_heads, splits);
+}
+
+size_t w4a16_tp_header_bytes(void) { return w4a16::kTpHeaderBytes; }
+
+size_t w4a16_tp_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int w4a16_tp_region_alloc(size_t out_bytes, void** region, void* ipc_handle) {
+  if (!region || !ipc_handle) {
+    set_error("null pointer argument");
+    return W4A16_ERR_NULL;
+  }
+  *region = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, w4a16::kTpHeaderBytes + out_bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, w4a16::kTpHeaderBytes + out_bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    set_error("tensor-parallel region of %zu bytes: %s", out_bytes, cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *region = p;
+  return W4A16_OK;
+}
+
+int w4a16_tp_region_open(const void* ipc_handle, void** region) {
+  if (!region || !ipc_handle) {
+    set_error("null pointer argument");
+    return W4A16_ERR_NULL;
+  }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  *region = p;
+  return W4A16_OK;
+}
+
+int w4a16_tp_region_close(void* region, int owned) {
+  if (!region) return W4A16_OK;
+  const cudaError_t e = owned ? cudaFree(region) : cudaIpcCloseMemHandle(region);
+  if (e != cudaSuccess) {
+    set_error("closing a tensor-parallel region: %s", cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  return W4A16_OK;
+}
+
+int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dtype, int group,
+                         const void* x, int rows, int cols, int out_dtype, long long row0, int rank,
+                         int nranks, void* const* regions, void* workspace, size_t workspace_bytes,
+                         unsigned flags, w4a16_stream_t stream) {
+  if (flags & ~(unsigned)W4A16_LAUNCH_PDL) {
+    set_error("unknown launch flags 0x%x", flags);
+    return W4A16_ERR_DTYPE;
+  }
+  if (!regions) {
+    set_error("null pointer argument");
+    return W4A16_ERR_NULL;
+  }
+  if (nranks < 2 || nranks > 8 || rank < 0 || rank >= nranks || row0 < 0 || rows < 1) {
+    set_error("fused all-gather needs 2..8 ranks, 0 <= rank < nranks, row0 >= 0 and rows >= 1 "
+              "(got rank %d of %d, row0 %lld, rows %d)", rank, nranks, row0, rows);
+    return W4A16_ERR_SHAPE;
+  }
+  for (int k = 0; k < nranks; ++k)
+    if (!regions[k] || !aligned(regions[k], 256)) {
+      set_error("region %d is null or not 256-byte aligned", k);
+      return regions[k] ? W4A16_ERR_ALIGN : W4A16_ERR_NULL;
+    }
+  uint8_t* mine = static_cast<uint8_t*>(regions[rank]) + w4a16::kTpHeaderBytes;
+  int rc = check_gemv(packed, W4A16_PACK_INTERLEAVED, scale, scale_dtype, group, x, 1, rows, cols,
+                      mine, out_dtype);
+  if (rc != W4A16_OK) return rc;
+  if (cols % 256 != 0 || !aligned(packed, 16)) {
+    set_error("fused all-gather needs cols %% 256 == 0 (got %d) and 16-byte aligned weights", cols);
+    return cols % 256 != 0 ? W4A16_ERR_SHAPE : W4A16_ERR_ALIGN;
+  }
+  w4a16::GemvProblem p;
+  p.packed = packed;
+  p.packing = W4A16_PACK_INTERLEAVED;
+  p.scale = scale;
+  p.scale_dtype = scale_dtype;
+  p.group = group;
+  p.x = x;
+  p.M = 1;
+  p.N = rows;
+  p.K = cols;
+  p.y = mine;
+  p.out_dtype = out_dtype;
+  p.workspace = workspace;
+  p.workspace_bytes = workspace ? workspace_bytes : 0;
+  p.tp_n = nranks;
+  p.tp_rank = rank;
+  p.tp_row0 = row0;
+  for (int k = 0; k < nranks; ++k) {
+    p.tp_flags[k] = static_cast<unsigned*>(regions[k]);
+    p.tp_out[k] = static_cast<uint8_t*>(regions[k]) + w4a16::kTpHeaderBytes;
+  }
+  p.pdl = (flags & W4A16_LAUNCH_PDL) != 0;
+  p.stream = reinterpret_cast<cudaStream_t>(stream);
+  return w4a16::launch_gemv(p);
 }
 
 size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols) {

@@ -190,6 +190,18 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
          ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
 }
 
+// ------------------------------------------------ flags shared with other GPUs
+// Release store / acquire load at system scope, for flags that peer GPUs read or write
+// through NVLink-mapped memory.
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ------------------------------------------------ programmatic dependent launch
 // A kernel launched with programmatic stream serialisation may start while the
 // previous kernel in the stream is still running.  grid_dependency_wait() returns once
@@ -253,8 +265,8 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
 }
 
 // 2-D tiled bulk tensor copy global -> shared, completion signalled on `bar`
-// (complete_tx).  No multicast: the source is always this GPU's own memory and
-// every CTA fetches its own tiles.
+// (complete_tx).  The source is always this GPU's own memory and every CTA fetches
+// its own tiles, one copy per CTA.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             uint32_t bar, uint64_t policy) {
   asm volatile(
@@ -264,7 +276,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// 3-D tiled bulk tensor copy global -> shared (no multicast), as tma_load_2d.
+// 3-D tiled bulk tensor copy global -> shared, one copy per CTA, as tma_load_2d.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y,
                                             int z, uint32_t bar, uint64_t policy) {
   asm volatile(

@@ -63,7 +63,18 @@ __device__ int g_device_error = 0;
 
 enum DeviceErrorCode : int {
   kDevErrStageTimeout = 1,  // a TMA stage did not land within the wait limit
+  kDevErrPeerTimeout = 2,   // a peer GPU's start or done flag did not arrive in time
 };
+
+// Fused all-gather (tensor parallel): every rank owns a region [header][gathered output];
+// the header holds, per source rank k, a start flag and a done flag (step epochs), this
+// rank's epoch, and a CTA-completion counter.  Peers write the flags through NVLink.
+constexpr int kMaxRanks = 8;
+constexpr int kTpStart = 0;                 // u32 [kMaxRanks]
+constexpr int kTpDone = kMaxRanks;          // u32 [kMaxRanks]
+constexpr int kTpEpoch = 2 * kMaxRanks;     // u32
+constexpr int kTpCtaDone = 2 * kMaxRanks + 1;
+constexpr uint64_t kPeerWaitLimitNs = 2000000000ull;  // 2 s
 
 constexpr uint64_t kStageWaitLimitNs = 2000000000ull;  // 2 s; a stage normally lands in us
 constexpr uint64_t kDrainWaitLimitNs = 100000000ull;   // 0.1 s per outstanding stage
@@ -98,6 +109,12 @@ struct TmaParams {
   const void* pro_src;     // prologue source (XM 2: fp32 h [K]; XM 3: fp16 gate|up [2K])
   const float* pro_gamma;  // XM 2: fp32 gamma [K]
   float pro_eps;           // XM 2: epsilon
+  // fused all-gather (tp_n > 1, one vector): rows go to row tp_row0 + r of every rank's
+  // gathered output tp_out[k]; tp_flags[k] is rank k's header
+  int tp_n, tp_rank;
+  long long tp_row0;
+  void* tp_out[kMaxRanks];
+  unsigned* tp_flags[kMaxRanks];
 };
 
 // How the single activation vector reaches shared memory (template parameter XM):
@@ -452,6 +469,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // next kernel be scheduled (it will overlap this one's tail).
   grid_dependency_wait();
   grid_launch_dependents();
+  // fused all-gather: per-CTA warp counter in the 128-byte scratch (bytes 64..67; the
+  // RMSNorm prologue uses only its first WARPS * 4 <= 64 bytes)
+  static_assert(WARPS * 4 <= 64, "scratch layout");
+  unsigned& tp_warps_done = *reinterpret_cast<unsigned*>(smem_raw + (xs - smem_addr(smem_raw)) + red_off + 64);
+  if (p.tp_n > 1) {
+    if (threadIdx.x == 0) tp_warps_done = 0u;  // a barrier follows before any warp counts
+    const unsigned e = *reinterpret_cast<volatile unsigned*>(p.tp_flags[p.tp_rank] + kTpEpoch) + 1u;
+    if (blockIdx.x == 0 && threadIdx.x < p.tp_n)
+      st_release_sys(p.tp_flags[threadIdx.x] + kTpStart + p.tp_rank, e);
+  }
 
   // kSchedLocal partial sums [unit of the CTA][16 rows] sit after the staged vector;
   // slots no segment starts at stay zero
@@ -572,7 +599,79 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     __syncthreads();
   }
 
-  if (!active && !local) return;
+  // Fused all-gather.  CTA 0 announces step tp_e to every rank (the previous kernel has
+  // completed, so this rank is done with the previous gathered output).  Each warp, before
+  // its first store into other ranks' buffers, waits until every rank has announced the
+  // step; the last warp of the last CTA publishes this rank's done flag to every rank,
+  // waits for all of theirs and advances this rank's epoch, so the kernel completes only
+  // when the whole gathered output is in place.  Every wait gives up after 2 s, records the
+  // error, and the warp then writes this rank's own buffer only.
+  const bool tp = p.tp_n > 1;
+  unsigned* tp_my = tp ? p.tp_flags[p.tp_rank] : nullptr;
+  const unsigned tp_e = tp ? *reinterpret_cast<volatile unsigned*>(tp_my + kTpEpoch) + 1u : 0u;
+  bool tp_started = false, tp_peers_ok = false;
+  auto tp_ensure_started = [&]() {  // warp-uniform
+    if (!tp || tp_started) return;
+    int ok = 1;
+    if (lane == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      for (int k = 0; k < p.tp_n && ok; ++k)
+        while ((int)(ld_acquire_sys(tp_my + kTpStart + k) - tp_e) < 0) {
+          if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+            record_device_error(kDevErrPeerTimeout);
+            ok = 0;
+            break;
+          }
+        }
+    }
+    tp_peers_ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
+    tp_started = true;
+  };
+  // One output element: the plain output, or row tp_row0 + r of every rank's buffer.
+  auto store_out = [&](size_t idx, int r, float v) {
+    if (!tp) {
+      static_cast<OT*>(p.y)[idx] = from_f32<OT>(v);
+      return;
+    }
+    const OT ov = from_f32<OT>(v);
+    if (tp_peers_ok) {
+      for (int k = 0; k < p.tp_n; ++k) static_cast<OT*>(p.tp_out[k])[p.tp_row0 + r] = ov;
+    } else {
+      static_cast<OT*>(p.tp_out[p.tp_rank])[p.tp_row0 + r] = ov;
+    }
+  };
+  auto tp_warp_done = [&]() {
+    if (!tp) return;
+    __syncwarp();
+    if (lane == 0) {
+      // Release chain: each warp's stores are ordered before its count (GPU-scope fence);
+      // the CTA's last warp, having observed every count, makes them visible at system
+      // scope before the grid-wide count, and the last CTA once more before the flags.
+      // (One system-scope fence per CTA instead of per warp: 68.2 -> 65.4 us per 2-GPU
+      // step.)
+      __threadfence();
+      if (atomicAdd(&tp_warps_done, 1u) == (unsigned)(WARPS - 1) &&
+          (__threadfence_system(), atomicAdd(tp_my + kTpCtaDone, 1u) == gridDim.x - 1)) {
+        tp_my[kTpCtaDone] = 0u;
+        __threadfence_system();
+        for (int k = 0; k < p.tp_n; ++k) st_release_sys(p.tp_flags[k] + kTpDone + p.tp_rank, tp_e);
+        const uint64_t t0 = globaltimer_ns();
+        for (int k = 0; k < p.tp_n; ++k)
+          while ((int)(ld_acquire_sys(tp_my + kTpDone + k) - tp_e) < 0) {
+            if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+              record_device_error(kDevErrPeerTimeout);
+              break;
+            }
+          }
+        tp_my[kTpEpoch] = tp_e;
+      }
+    }
+  };
+
+  if (!active && !local) {
+    tp_warp_done();
+    return;
+  }
 
   float tot[RT][NH][4];
   float acc[RT][2][NH][4];
@@ -616,6 +715,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       for (int s = consumed + 1; s < issued; ++s)
         mbar_wait_bounded(bar0 + 8 * (s % STAGES), (s / STAGES) & 1u, kDrainWaitLimitNs);
       if (local) break;  // the CTA still meets at the reduction barrier
+      tp_warp_done();
       return;
     }
     const uint32_t wbase = wring + slot * L::kWStride;
@@ -664,6 +764,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     // Fragment (rt, h, i): row cur_tile*kRows + rt*16 + g (+8 for i >= 2), batch
     // column n = h*8 + 2t + (i & 1).
     if (tile_w0 == 0 && tile_done) {  // the whole tile was summed here
+      tp_ensure_started();
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -676,7 +777,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             if (ok && r < p.N) {
               float v = tot[rt][h][i];
               if (p.bias) v += __ldcg(p.bias + r);  // may be the previous kernel's output
-              static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
+              store_out((size_t)n * p.N + r, r, v);
             }
           }
       continue;
@@ -719,6 +820,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (prev != (unsigned)(w_last - w_first)) continue;
     __threadfence();
+    tp_ensure_started();
     // Every contributor after the first starts inside this tile, so the tile is its
     // first (slot 0); the first contributor used slot 1 unless it also started here.
     const int slot_first = ((long long)w_first * U / T) / nwin == cur_tile ? 0 : 1;
@@ -738,7 +840,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             float v = __ldcg(p.partial + ((size_t)w_first * 2 + slot_first) * p.M * kRows + off);
             for (int w = w_first + 1; w <= w_last; ++w) v += __ldcg(p.partial + (size_t)w * wstride + off);
             if (p.bias) v += __ldcg(p.bias + r);  // may be the previous kernel's output
-            static_cast<OT*>(p.y)[(size_t)n * p.N + r] = from_f32<OT>(v);
+            store_out((size_t)n * p.N + r, r, v);
           }
         }
     __syncwarp();
@@ -748,6 +850,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     // Tiles split between warps of this CTA: add their segments in window order.
     if constexpr (NB == 1) {
       __syncthreads();
+      tp_ensure_started();
       for (int i = threadIdx.x; i < ntl * kRows; i += blockDim.x) {
         const int tl = i / kRows, rl = i - tl * kRows;
         const long long tu0 = (long long)tl * nwin;
@@ -757,9 +860,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         float v = 0.f;
         for (int w = 0; w < nwin; ++w) v += lpart[(tl * nwin + w) * kRows + rl];
         if (p.bias) v += __ldcg(p.bias + r);
-        static_cast<OT*>(p.y)[r] = from_f32<OT>(v);
+        store_out(r, r, v);
       }
     }
+    tp_warp_done();
     return;
   }
   if (dyn && lane == 0) {
@@ -770,6 +874,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       p.counters[kDoneWarpCounter] = 0u;
     }
   }
+  tp_warp_done();
 }
 
 // ------------------------------------------------------------ generic fallback
@@ -1028,6 +1133,13 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   prm.pro_src = p.pro_src;
   prm.pro_gamma = p.pro_gamma;
   prm.pro_eps = p.pro_eps;
+  prm.tp_n = p.tp_n;
+  prm.tp_rank = p.tp_rank;
+  prm.tp_row0 = p.tp_row0;
+  for (int k = 0; k < kMaxRanks; ++k) {
+    prm.tp_out[k] = p.tp_out[k];
+    prm.tp_flags[k] = p.tp_flags[k];
+  }
   prm.partial = nullptr;
   prm.counters = nullptr;
   if (have_ws && prm.sched != kSchedLocal) {
@@ -1067,6 +1179,11 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
       (PACK == W4A16_PACK_INTERLEAVED ||
        (GS == 0 && std::is_same<ST, float>::value && std::is_same<OT, float>::value)) &&
       StageLayout<kSlabs, kRT, GS, ST>::kScaleBoxOk;
+  if (p.tp_n > 1 && (!kTmaVariant || !use_tma || M != 1 || PACK != W4A16_PACK_INTERLEAVED)) {
+    set_error("the fused all-gather needs one activation vector on the TMA path: cols %% 256 == 0, "
+              "16-byte aligned weights, interleaved packing");
+    return W4A16_ERR_SHAPE;
+  }
   if (p.staged && (!kTmaVariant || !use_tma)) {
     set_error("the staged (fused) GEMV needs the TMA path: cols %% 256 == 0, 16-byte aligned "
               "weights, interleaved packing");

@@ -33,6 +33,11 @@ struct GemvProblem {
   const void* pro_src = nullptr;
   const float* pro_gamma = nullptr;
   float pro_eps = 0.f;
+  int tp_n = 0;                     // fused all-gather over tp_n ranks (0: plain output y)
+  int tp_rank = 0;
+  long long tp_row0 = 0;            // this rank's first row in the gathered output
+  void* tp_out[8] = {};             // every rank's gathered output
+  unsigned* tp_flags[8] = {};       // every rank's region header
   bool staged = false;              // fused entry: x staged in shared memory, TMA kernel only
   bool pdl = false;                 // programmatic dependent launch (staged GEMV only)
   cudaStream_t stream = nullptr;
@@ -92,6 +97,9 @@ cudaError_t launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
+
+// Fused all-gather: bytes of the flag header at the start of every rank's region.
+constexpr size_t kTpHeaderBytes = 256;
 
 // Reads (and clears) the device-side error word written by kernels whose bounded
 // waits ran out.  Synchronises `stream`.

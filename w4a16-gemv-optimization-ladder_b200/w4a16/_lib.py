@@ -45,6 +45,13 @@ SIGNATURES = {
                          _i),
     "w4a16_decode_attention": ([_p, _p, _p, _p, _p, _p, _p, _p, _sz, _i, _i, _i, _i, _i, _u, _p], _i),
     "w4a16_decode_attention_scratch_bytes": ([_i, _i, _i], _sz),
+    "w4a16_tp_header_bytes": ([], _sz),
+    "w4a16_tp_ipc_handle_bytes": ([], _sz),
+    "w4a16_tp_region_alloc": ([_sz, ctypes.POINTER(ctypes.c_void_p), _p], _i),
+    "w4a16_tp_region_open": ([_p, ctypes.POINTER(ctypes.c_void_p)], _i),
+    "w4a16_tp_region_close": ([_p, _i], _i),
+    "w4a16_gemv_allgather": ([_p, _p, _i, _i, _p, _i, _i, _i, ctypes.c_longlong, _i, _i,
+                              ctypes.POINTER(ctypes.c_void_p), _p, _sz, _u, _p], _i),
     "w4a16_gemv_noalloc": ([_p, _p, _i, _i, _p, _i, _i, _p, _p], _i),
     "w4a16_dequant": ([_p, _i, _p, _i, _i, _i, _i, _p, _p], _i),
     "w4a16_quantize_pack": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p], _i),

@@ -9,7 +9,13 @@ split is the only exchange: no partial sums cross GPUs.
 
 Shard boundaries are rounded to multiples of 16 rows (the kernel's tile) so that
 every rank's slice starts on a tile; the last rank takes the remainder.
+
+FusedAllGatherW4A16 does the same for one activation vector without NCCL: the GEMV's
+epilogue stores each output row into every rank's gathered buffer through NVLink
+(CUDA IPC mappings of the peers' buffers), with step flags in the same buffers.
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -87,3 +93,110 @@ class RowShardedW4A16:
             if hi > lo:
                 full[:, lo:hi] = gathered[r, :, : hi - lo]
         return full.view(-1) if x.dim() == 1 and out is None else full
+
+
+class _DeviceArray:
+    """A raw device allocation seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr, n, dtype):
+        typestr = {torch.float32: "<f4", torch.float16: "<f2"}[dtype]
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class FusedAllGatherW4A16:
+    """Row shard of an int4 weight whose GEMV writes straight into every rank's output.
+
+    Each rank allocates one region (header + the full [rows] output) with the library,
+    shares its CUDA IPC handle over `process_group`, and opens the other ranks' regions;
+    __call__(x) then runs w4a16_gemv_allgather: this rank's rows land in all ranks'
+    outputs, and the call returns when (on the stream) every rank has finished the step.
+    The returned tensor is the same buffer every call (valid until the next call).
+    One activation vector (fp16 [K]); 2..8 ranks; interleaved packing.
+    """
+
+    def __init__(self, packed_shard, scale_shard, rows, group=0, process_group=None,
+                 out_dtype=torch.float32, lib=None):
+        from . import _lib
+        from . import kernels as K
+
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        if not 2 <= self.world <= 8:
+            raise ValueError(f"the fused all-gather takes 2..8 ranks, got {self.world}")
+        self.rows, self.group, self.out_dtype = rows, group, out_dtype
+        self.packed, self.scale = packed_shard, scale_shard
+        self.lo, self.hi = shard_bounds(rows, self.world, self.rank)
+        if packed_shard.shape[0] != self.hi - self.lo or self.hi <= self.lo:
+            raise ValueError(f"rank {self.rank} owns rows [{self.lo},{self.hi}) but got {packed_shard.shape[0]}")
+        self._check = _lib.check
+        self.lib = lib or _lib.lib()
+        esize = 4 if out_dtype == torch.float32 else 2
+        self._odt = _lib.DTYPE_F32 if out_dtype == torch.float32 else _lib.DTYPE_F16
+        handle = ctypes.create_string_buffer(int(self.lib.w4a16_tp_ipc_handle_bytes()))
+        mine = ctypes.c_void_p()
+        self._check(self.lib.w4a16_tp_region_alloc(rows * esize, ctypes.byref(mine), handle),
+                    "w4a16_tp_region_alloc")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.raw), group=process_group)
+        self.regions = []
+        for k, h in enumerate(handles):
+            if k == self.rank:
+                self.regions.append(mine.value)
+                continue
+            ptr = ctypes.c_void_p()
+            self._check(self.lib.w4a16_tp_region_open(ctypes.create_string_buffer(h, len(h)),
+                                                       ctypes.byref(ptr)), "w4a16_tp_region_open")
+            self.regions.append(ptr.value)
+        self._regions = (ctypes.c_void_p * self.world)(*self.regions)
+        dist.barrier(group=process_group)  # every rank holds every mapping before the first step
+        self.device = packed_shard.device
+        self.out = self._make_out(mine.value + int(self.lib.w4a16_tp_header_bytes()), rows, out_dtype)
+        # two split-K workspaces: chained (pdl) launches overlap neighbours, which must not share one
+        self.workspaces = [K.new_workspace(self.device) for _ in range(2)] if self.device.type == "cuda" else None
+        self._step = 0
+        self._closed = False
+
+    def _make_out(self, ptr, n, dtype):
+        return torch.as_tensor(_DeviceArray(ptr, n, dtype), device=self.device)
+
+    def launch(self, packed, scale, x, stream=None, pdl=False):
+        """One step with explicit weights (this rank's rows), for callers that alternate
+        several weight copies of the same shape.  pdl: chain to the previous kernel on the
+        stream (programmatic dependent launch); the workspaces alternate per call."""
+        from . import _lib
+        from . import kernels as K
+
+        s = stream if stream is not None else K._stream(self.device)
+        ws = self.workspaces[self._step % 2] if self.workspaces is not None else None
+        self._step += 1
+        st = self.lib.w4a16_gemv_allgather(
+            ctypes.c_void_p(packed.data_ptr()), ctypes.c_void_p(scale.data_ptr()),
+            0 if scale.dtype == torch.float32 else 1, self.group, ctypes.c_void_p(x.data_ptr()),
+            packed.shape[0], packed.shape[1] * 2, self._odt, self.lo, self.rank, self.world,
+            self._regions, ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
+            ws.numel() if ws is not None else 0, _lib.LAUNCH_PDL if pdl else 0, s)
+        self._check(st, "w4a16_gemv_allgather")
+        return self.out
+
+    def __call__(self, x, pdl=False):
+        if not (isinstance(x, torch.Tensor) and x.dtype == torch.float16 and x.dim() == 1
+                and x.is_contiguous() and x.shape[0] == self.packed.shape[1] * 2 and x.device == self.device):
+            raise RuntimeError("x must be a contiguous fp16 [cols] tensor on this rank's device")
+        with torch.cuda.device(self.device):
+            return self.launch(self.packed, self.scale, x, pdl=pdl)
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (after every rank is done)."""
+        if self._closed:
+            return
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.pg)
+        for k, ptr in enumerate(self.regions):
+            if k != self.rank:
+                self.lib.w4a16_tp_region_close(ctypes.c_void_p(ptr), 0)
+        dist.barrier(group=self.pg)
+        self.lib.w4a16_tp_region_close(ctypes.c_void_p(self.regions[self.rank]), 1)
+        self._closed = True
