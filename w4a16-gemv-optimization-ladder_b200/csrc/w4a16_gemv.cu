@@ -347,7 +347,7 @@ __device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
 }
 
 template <int PACK, int GS, typename ST, int NB, typename OT, int WARPS, int STAGES, int SLABS, int RT,
-          int XM>
+          int XM, bool TP = false>
 __global__ void __launch_bounds__(WARPS * 32, 1)
     k_gemv_tma(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const TmaParams p) {
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // RMSNorm prologue uses only its first WARPS * 4 <= 64 bytes)
   static_assert(WARPS * 4 <= 64, "scratch layout");
   unsigned& tp_warps_done = *reinterpret_cast<unsigned*>(smem_raw + (xs - smem_addr(smem_raw)) + red_off + 64);
-  if (p.tp_n > 1) {
+  if (TP && p.tp_n > 1) {
     if (threadIdx.x == 0) tp_warps_done = 0u;  // a barrier follows before any warp counts
     const unsigned e = *reinterpret_cast<volatile unsigned*>(p.tp_flags[p.tp_rank] + kTpEpoch) + 1u;
     if (blockIdx.x == 0 && threadIdx.x < p.tp_n)
@@ -606,7 +606,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // waits for all of theirs and advances this rank's epoch, so the kernel completes only
   // when the whole gathered output is in place.  Every wait gives up after 2 s, records the
   // error, and the warp then writes this rank's own buffer only.
-  const bool tp = p.tp_n > 1;
+  const bool tp = TP && p.tp_n > 1;  // the fused all-gather is compiled only into TP kernels
   unsigned* tp_my = tp ? p.tp_flags[p.tp_rank] : nullptr;
   const unsigned tp_e = tp ? *reinterpret_cast<volatile unsigned*>(tp_my + kTpEpoch) + 1u : 0u;
   bool tp_started = false, tp_peers_ok = false;
@@ -1035,10 +1035,10 @@ int tail_smem_bytes(int K) {
   return (XM != kXGlobal ? K * 2 : 0) + (NB == 1 ? 128 : 0) + corr;
 }
 
-template <int PACK, int GS, typename ST, int NB, typename OT, int XM>
+template <int PACK, int GS, typename ST, int NB, typename OT, int XM, bool TP = false>
 int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
   using L = StageLayout<kSlabs, kRT, GS, ST>;
-  auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM>;
+  auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM, TP>;
   const int smem_base = tma_smem_bytes<GS, ST>() + tail_smem_bytes<PACK, NB, XM>(p.K);
   int smem = smem_base;
   if (smem > di.smem_optin) {
@@ -1218,6 +1218,12 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
   }
   if (M == 1) {
     // one activation vector: keep it in shared memory when it fits beside the ring
+    if constexpr (PACK == W4A16_PACK_INTERLEAVED) {
+      if (p.tp_n > 1) {
+        if (xs_fits) return launch_tma<PACK, GS, ST, 1, OT, kXCopy, true>(p, x, M, y, di, dev);
+        return launch_tma<PACK, GS, ST, 1, OT, kXGlobal, true>(p, x, M, y, di, dev);
+      }
+    }
     if (xs_fits) return launch_tma<PACK, GS, ST, 1, OT, kXCopy>(p, x, M, y, di, dev);
     return launch_tma<PACK, GS, ST, 1, OT, kXGlobal>(p, x, M, y, di, dev);
   }
