@@ -190,6 +190,31 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
          ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
 }
 
+// Raw bits of a scale, loaded where the call stands (volatile: the compiler may not
+// sink the load to the value's first use), for scales used much later.
+template <typename T>
+__device__ __forceinline__ uint32_t ld_scale_bits_now(const T* p);
+template <>
+__device__ __forceinline__ uint32_t ld_scale_bits_now<float>(const float* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+template <>
+__device__ __forceinline__ uint32_t ld_scale_bits_now<__half>(const __half* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.b16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+template <typename T>
+__device__ __forceinline__ float scale_from_bits(uint32_t b);
+template <>
+__device__ __forceinline__ float scale_from_bits<float>(uint32_t b) { return __uint_as_float(b); }
+template <>
+__device__ __forceinline__ float scale_from_bits<__half>(uint32_t b) {
+  return __half2float(__ushort_as_half((unsigned short)b));
+}
+
 // ------------------------------------------------ flags shared with other GPUs
 // Release store / acquire load at system scope, for flags that peer GPUs read or write
 // through NVLink-mapped memory.

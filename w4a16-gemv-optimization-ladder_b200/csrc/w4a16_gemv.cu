@@ -675,7 +675,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
   float tot[RT][NH][4];
   float acc[RT][2][NH][4];
-  float srow[RT][2];
+  uint32_t srow_bits[RT][2];  // per-row scales (raw bits), converted in the epilogue
   int tile = first_tile, win = first_win, tile_w0 = first_win;
 
 #pragma unroll 1
@@ -699,11 +699,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             acc[rt][1][h][i] = 0.f;
           }
         const int r0 = tile * kRows + rt * 16 + g;
-        srow[rt][0] = srow[rt][1] = 1.f;
-        if (!GS) {  // per-row scales are used in the epilogue: fetch them now
+        if (!GS) {  // per-row scales are used in the epilogue: issue the loads now
           const ST* sr = static_cast<const ST*>(p.scale_rows);
-          if (r0 < p.N) srow[rt][0] = to_f32<ST>(__ldg(sr + r0));
-          if (r0 + 8 < p.N) srow[rt][1] = to_f32<ST>(__ldg(sr + r0 + 8));
+          srow_bits[rt][0] = r0 < p.N ? ld_scale_bits_now<ST>(sr + r0) : 0u;
+          srow_bits[rt][1] = r0 + 8 < p.N ? ld_scale_bits_now<ST>(sr + r0 + 8) : 0u;
         }
       }
     }
@@ -740,6 +739,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (!tile_done && (dyn || consumed + 1 < count)) continue;  // the tile goes on here
 
     // ---- tile epilogue
+    float srow[RT][2];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt) {
+      srow[rt][0] = GS ? 1.f : scale_from_bits<ST>(srow_bits[rt][0]);
+      srow[rt][1] = GS ? 1.f : scale_from_bits<ST>(srow_bits[rt][1]);
+    }
     if (!GS && FOLD) {  // the groups were summed into tot: apply the row scale
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
