@@ -526,7 +526,9 @@ def run_reference(args, rank, world):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(us_full / 1000.0, 3), "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "g128 int4 GEMV 262144x2048, batch 1, CPU"},
+            "config": {"workload": "g128 int4 GEMV 262144x2048, batch 1", "rows_per_gpu": ROWS,
+                       "cols": COLS, "group": GROUP,
+                       "parallelism": "host cores of rank 0 (the reference's CPU path)"},
             "cpu_baseline": {"value": round(us_full, 1), "unit": "µs", "cores": threads,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(us_full, 1), "unit": "µs", "h2d_bytes_per_step": 0,
