@@ -149,7 +149,9 @@ def _attention_ref(qkv, cos, sin, pos, kc, vc, heads, kv_heads):
 
 @pytest.mark.parametrize("heads,kv_heads,max_len,pos,splits", [
     (32, 8, 512, 511, None), (32, 8, 512, 0, None), (32, 8, 512, 200, 1), (32, 8, 128, 63, 128),
-    (8, 8, 256, 100, 3), (4, 1, 96, 95, 5), (32, 1, 64, 40, 2), (32, 8, 4096, 3000, None)])
+    (8, 8, 256, 100, 3), (4, 1, 96, 95, 5), (32, 1, 64, 40, 2), (32, 8, 4096, 3000, None),
+    # one CTA per kv head (splits 1, cache <= 512, 1/2/4/8 query heads per kv head)
+    (8, 1, 512, 300, 1), (16, 8, 384, 383, 1), (8, 8, 64, 10, 1), (32, 8, 512, 33, 1)])
 def test_decode_attention_matches_fp32_reference(heads, kv_heads, max_len, pos, splits):
     torch.manual_seed(heads + max_len + pos)
     qkv = torch.randn((heads + 2 * kv_heads) * 64, device="cuda").half()
@@ -180,9 +182,13 @@ def test_decode_attention_repeatable_and_scratch_left_zeroed():
     vc = torch.randn_like(kc)
     cos, sin = _rope_tables(max_len)
     p = torch.tensor([300], device="cuda")
-    a = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads).clone()
-    b = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads).clone()
+    a = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads, splits=1).clone()
+    b = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads, splits=1).clone()
     assert torch.equal(a, b)
+    b = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads, splits=16).clone()
+    c = K.decode_attention(qkv, cos, sin, p, kc, vc, heads=heads, kv_heads=kv_heads, splits=16).clone()
+    assert torch.equal(b, c)                                      # split path: repeatable too
+    assert (a.float() - b.float()).abs().max().item() < 2e-3      # and equal to the one-CTA path
     scratch = K.kernels._ATTN_SCRATCH[(0, heads, kv_heads, 16)]
     assert int(scratch[-kv_heads * 4:].count_nonzero()) == 0   # per-kv-head counters back at zero
 
@@ -195,11 +201,12 @@ def test_decode_attention_position_out_of_range():
     kc0, vc0 = kc.clone(), vc.clone()
     cos, sin = _rope_tables(max_len)
     for bad in (max_len, -1):
-        out = K.decode_attention(qkv, cos, sin, torch.tensor([bad], device="cuda"), kc, vc,
-                                 heads=heads, kv_heads=kv_heads, splits=4)
-        torch.cuda.synchronize()
-        assert torch.isnan(out).all()
-        assert torch.equal(kc, kc0) and torch.equal(vc, vc0)
+        for splits in (4, 1):  # the split kernel and the one-CTA kernel
+            out = K.decode_attention(qkv, cos, sin, torch.tensor([bad], device="cuda"), kc, vc,
+                                     heads=heads, kv_heads=kv_heads, splits=splits)
+            torch.cuda.synchronize()
+            assert torch.isnan(out).all()
+            assert torch.equal(kc, kc0) and torch.equal(vc, vc0)
     good = K.decode_attention(qkv, cos, sin, torch.tensor([10], device="cuda"), kc, vc,
                               heads=heads, kv_heads=kv_heads, splits=4)
     assert torch.isfinite(good).all()

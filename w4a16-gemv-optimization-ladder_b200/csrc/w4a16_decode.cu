@@ -265,6 +265,158 @@ __global__ void __launch_bounds__(MAXT) k_decode_attention(const __half* qkv, co
   if (threadIdx.x == 0) counters[kvh] = 0u;
 }
 
+// One CTA per kv head for a cache of at most kCtaWarps * 32 positions and G query heads
+// per kv head: warp w takes positions [32w, 32w + 32) for all G heads (one key row per
+// lane), and the 16 warps' partial softmaxes are combined in shared memory, so nothing
+// but the output leaves the CTA.  The key and value rows below pos are fetched before the
+// dependency wait (earlier steps wrote them); warp G writes the new row at pos.
+constexpr int kCtaWarps = 16;
+
+template <int G>
+__global__ void __launch_bounds__(kCtaWarps * 32)
+    k_decode_attention_cta(const __half* qkv, const float* __restrict__ cos_t,
+                           const float* __restrict__ sin_t, const long long* __restrict__ pos_p,
+                           __half* k_cache, __half* v_cache, __half* __restrict__ out, int heads,
+                           int kv_heads, int max_len, float scale) {
+  static_assert(G >= 1 && G < kCtaWarps, "query heads per kv head");
+  constexpr int kPart = kHeadDim + 2;
+  const int kvh = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long pos_ll = pos_p[0];  // set before the step
+  const bool bad_pos = pos_ll < 0 || pos_ll >= max_len;
+  const int pos = bad_pos ? 0 : (int)pos_ll;
+  const int jend = bad_pos ? 0 : pos + 1;  // positions [0, pos] take part
+  const int j0 = warp * 32;
+  const int j = j0 + lane;
+  const int nvalid = max(0, min(32, jend - j0));
+  __half* kc = k_cache + (size_t)kvh * max_len * kHeadDim;
+  __half* vc = v_cache + (size_t)kvh * max_len * kHeadDim;
+
+  uint4 kreg[8];
+  __half2 vreg[32];
+  if (j < jend && j != pos) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kc + (size_t)j * kHeadDim);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) kreg[e] = kr[e];
+  }
+  {
+    const __half2* vr = reinterpret_cast<const __half2*>(vc + (size_t)j0 * kHeadDim) + lane;
+#pragma unroll
+    for (int u = 0; u < 32; ++u)
+      if (u < nvalid && j0 + u != pos) vreg[u] = vr[u * (kHeadDim / 2)];
+  }
+
+  grid_dependency_wait();
+  grid_launch_dependents();
+  if (bad_pos) {  // nothing is read or written: the heads read NaN
+    if (warp < G) {
+      const __half2 nan2 = __float2half2_rn(__int_as_float(0x7fc00000));
+      reinterpret_cast<__half2*>(out + (kvh * G + warp) * kHeadDim)[lane] = nan2;
+    }
+    return;
+  }
+
+  extern __shared__ float sm[];  // q [G][64] (rotated, scaled) | k_new [64] | v_new [64] | parts [warps][G][66]
+  float* qs = sm;
+  float* kn = qs + G * kHeadDim;
+  float* vn = kn + kHeadDim;
+  float* parts = vn + kHeadDim;
+  const float* cr = cos_t + (size_t)pos * kHeadDim;
+  const float* sr = sin_t + (size_t)pos * kHeadDim;
+  if (warp < G) {  // rotate query head kvh * G + warp
+    const int head = kvh * G + warp;
+    float a = __half2float(__ldcg(qkv + head * kHeadDim + lane));
+    float b = __half2float(__ldcg(qkv + head * kHeadDim + lane + 32));
+    rope_pair(a, b, cr, sr, lane);
+    qs[warp * kHeadDim + lane] = a * scale;
+    qs[warp * kHeadDim + lane + 32] = b * scale;
+  } else if (warp == G) {  // the new key (rotated) and value, into the cache and smem
+    const int kb = heads * kHeadDim + kvh * kHeadDim;
+    const int vb = (heads + kv_heads) * kHeadDim + kvh * kHeadDim;
+    float a = __half2float(__ldcg(qkv + kb + lane));
+    float b = __half2float(__ldcg(qkv + kb + lane + 32));
+    rope_pair(a, b, cr, sr, lane);
+    const __half ah = __float2half_rn(a), bh = __float2half_rn(b);
+    const __half va = __ldcg(qkv + vb + lane), vb2 = __ldcg(qkv + vb + lane + 32);
+    kc[(size_t)pos * kHeadDim + lane] = ah;
+    kc[(size_t)pos * kHeadDim + lane + 32] = bh;
+    vc[(size_t)pos * kHeadDim + lane] = va;
+    vc[(size_t)pos * kHeadDim + lane + 32] = vb2;
+    kn[lane] = __half2float(ah);
+    kn[lane + 32] = __half2float(bh);
+    vn[lane] = __half2float(va);
+    vn[lane + 32] = __half2float(vb2);
+  }
+  __syncthreads();
+
+  // this warp's block for every query head of the group
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    const float* q = qs + h * kHeadDim;
+    float sc = -INFINITY;
+    if (j < jend) {
+      float d = 0.f;
+      if (j == pos) {
+#pragma unroll 8
+        for (int e = 0; e < kHeadDim; ++e) d = fmaf(q[e], kn[e], d);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t w4[4] = {kreg[e].x, kreg[e].y, kreg[e].z, kreg[e].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+            d = fmaf(q[e * 8 + 2 * i], f.x, d);
+            d = fmaf(q[e * 8 + 2 * i + 1], f.y, d);
+          }
+        }
+      }
+      sc = d;
+    }
+    const float m = warp_max(sc);
+    const float pj = sc == -INFINITY ? 0.f : __expf(sc - m);
+    const float l = warp_sum(pj);
+    float2 o = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 32; ++u) {
+      if (u < nvalid) {
+        const float pu = __shfl_sync(0xffffffffu, pj, u);
+        const float2 v = j0 + u == pos ? make_float2(vn[2 * lane], vn[2 * lane + 1])
+                                       : __half22float2(vreg[u]);
+        o.x = fmaf(pu, v.x, o.x);
+        o.y = fmaf(pu, v.y, o.y);
+      }
+    }
+    float* part = parts + (warp * G + h) * kPart;
+    if (lane == 0) {
+      part[0] = m;  // -inf for a block past pos
+      part[1] = l;
+    }
+    reinterpret_cast<float2*>(part + 2)[lane] = o;
+  }
+  __syncthreads();
+
+  if (warp < G) {  // head kvh * G + warp: combine the blocks in warp order
+    const int h = warp;
+    const float mw = lane < kCtaWarps ? parts[(lane * G + h) * kPart] : -INFINITY;
+    const float M = warp_max(mw);
+    const float ww = mw == -INFINITY ? 0.f : __expf(mw - M);
+    const float lw = lane < kCtaWarps ? parts[(lane * G + h) * kPart + 1] * ww : 0.f;
+    float L = 0.f;
+    float2 a = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kCtaWarps; ++w) {
+      const float wu = __shfl_sync(0xffffffffu, ww, w);
+      L += __shfl_sync(0xffffffffu, lw, w);
+      const float2 ov = reinterpret_cast<const float2*>(parts + (w * G + h) * kPart + 2)[lane];
+      a.x = fmaf(ov.x, wu, a.x);
+      a.y = fmaf(ov.y, wu, a.y);
+    }
+    reinterpret_cast<__half2*>(out + (kvh * G + h) * kHeadDim)[lane] = __floats2half2_rn(a.x / L, a.y / L);
+  }
+}
+
 }  // namespace
 
 size_t decode_attention_scratch_bytes(int heads, int kv_heads, int splits) {
@@ -276,6 +428,23 @@ int launch_decode_attention(const void* qkv, const float* cos_t, const float* si
                             void* scratch, int heads, int kv_heads, int head_dim, int max_len,
                             int splits, bool pdl, cudaStream_t stream) {
   const int group = heads / kv_heads;
+  if (splits == 1 && max_len <= kCtaWarps * 32 && (group == 1 || group == 2 || group == 4 || group == 8)) {
+    // the whole cache of a kv head in one CTA: combine in shared memory
+    const size_t csmem = ((size_t)(group + 2) * kHeadDim + (size_t)kCtaWarps * group * (kHeadDim + 2)) * 4;
+    auto ck = group == 1 ? k_decode_attention_cta<1>
+                         : group == 2 ? k_decode_attention_cta<2>
+                                      : group == 4 ? k_decode_attention_cta<4> : k_decode_attention_cta<8>;
+    cudaError_t e = launch_maybe_pdl(
+        ck, dim3(kv_heads), dim3(kCtaWarps * 32), csmem, stream, pdl, static_cast<const __half*>(qkv),
+        cos_t, sin_t, pos, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache),
+        static_cast<__half*>(out), heads, kv_heads, max_len, 1.0f / sqrtf((float)head_dim));
+    (void)cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_error("k_decode_attention_cta launch failed: %s", cudaGetErrorString(e));
+      return W4A16_ERR_CUDA;
+    }
+    return W4A16_OK;
+  }
   const size_t smem = (size_t)(group + 2) * kHeadDim * 4;
   // up to 8 query heads per kv head (256 threads) the prefetch keeps its registers;
   // larger groups run with the register cap of 1024-thread blocks

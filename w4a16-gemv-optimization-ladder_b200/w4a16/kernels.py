@@ -233,7 +233,8 @@ def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, o
     (rotate-half tables); pos int64 [1] on the device; k_cache, v_cache fp16
     [kv_heads, max_len, 64] (this layer's).  Writes k_cache/v_cache at pos and returns
     out fp16 [heads * 64].  splits: CTAs per kv head over the positions (default one per
-    32 positions).  The zeroed scratch is kept per device and shape; allocate it (one
+    32 positions; splits=1 with max_len <= 512 and 1, 2, 4 or 8 query heads per kv head
+    runs one 16-warp CTA per kv head that combines in shared memory).  The zeroed scratch is kept per device and shape; allocate it (one
     eager call) before capturing the op in a CUDA graph.  pdl: programmatic dependent
     launch (see gemv_staged)."""
     dev = qkv.device
@@ -248,7 +249,7 @@ def decode_attention(qkv, cos, sin, pos, k_cache, v_cache, *, heads, kv_heads, o
         _need(t.device == dev and t.dtype == torch.float32 and t.is_contiguous()
               and t.dim() == 2 and t.shape[1] == D and t.shape[0] >= max_len, f"{name} must be fp32 [>= max_len, 64]")
     _need(pos.device == dev and pos.dtype == torch.int64 and pos.numel() == 1, "pos must be int64 [1] on the device")
-    if splits is None:
+    if splits is None:  # one CTA per 32 positions (the fastest measured split for one token)
         splits = max(1, (max_len + 31) // 32)
     if out is None:
         out = torch.empty(heads * D, dtype=torch.float16, device=dev)
