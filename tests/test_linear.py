@@ -4,6 +4,8 @@ CPU: the swap bookkeeping (which modules, buffers, shapes) on a small random Lla
 GPU: forward parity of the swapped layers against the oracle, the reference's
 113-Linear swap count on a random-init Llama-3.2-1B-architecture model, and the
 batch paths (kernel for <= 64 rows, dense or dequantised fallback above)."""
+import copy
+
 import numpy as np
 import pytest
 import torch
@@ -105,3 +107,20 @@ def test_linear_three_dim_input_and_bf16():
     q = O.unpack_int4(layer.packed.cpu().numpy())
     ref = O.gemv(q, layer.scale.cpu().numpy(), x.reshape(6, 512).half().cpu().numpy(), 128)
     assert np.abs(y.reshape(6, 256).float().cpu().numpy() - ref).max() < 3e-2  # bf16 output rounding
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("group,scale_dtype", [(0, torch.float32), (128, torch.float32), (128, torch.float16)])
+def test_gpu_quantizer_swap_is_bit_identical(group, scale_dtype):
+    # replace_linear_with_w4a16(quantizer="gpu") quantises and packs in one launch per layer
+    # against the torch quantiser on the host (the reference's path; torch's CUDA division
+    # is not always correctly rounded, the kernel's is)
+    torch.manual_seed(4)
+    base = nn.Sequential(nn.Linear(2048, 3072), nn.Sequential(nn.Linear(3072, 256, bias=False))).half()
+    a = copy.deepcopy(base)          # weights on the CPU: torch quantises there, buffers go to cuda
+    b = copy.deepcopy(base).cuda()
+    K.replace_linear_with_w4a16(a, group=group, keep_dense=False, scale_dtype=scale_dtype, device="cuda")
+    K.replace_linear_with_w4a16(b, group=group, keep_dense=False, scale_dtype=scale_dtype, quantizer="gpu")
+    for la, lb in ((a[0], b[0]), (a[1][0], b[1][0])):
+        assert torch.equal(la.packed, lb.packed)
+        assert la.scale.dtype == lb.scale.dtype == scale_dtype and torch.equal(la.scale, lb.scale)

@@ -25,6 +25,7 @@ from .kernels import (
     w4a16_gemv,
     w4a16_gemv_g128,
 )
+from .checkpoint import load_quantized, save_quantized
 from .linear import W4A16Linear, replace_linear_with_w4a16
 from .quant import (
     dequant_ref,
@@ -44,6 +45,7 @@ __all__ = [
     "dequant_ref", "dequant_ref_group", "W4A16Linear", "replace_linear_with_w4a16",
     # additions
     "gemv", "gemv_staged", "gemv_rmsnorm", "gemv_swiglu", "decode_attention", "new_workspace",
-    "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace",
+    "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace", "save_quantized",
+    "load_quantized",
     "read_device_error",
 ]

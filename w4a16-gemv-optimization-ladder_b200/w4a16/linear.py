@@ -61,13 +61,17 @@ class W4A16Linear(nn.Module):
 
 
 def replace_linear_with_w4a16(module, group=0, keep_dense=True, scale_dtype=torch.float32,
-                              device=None):
+                              device=None, quantizer="torch"):
     """Swap every nn.Linear under `module` for a W4A16Linear (reference kernels.py:127-137).
 
     Defaults match the reference: per-row scales, the dense fp16 weight kept for large
     batches, buffers on the GPU.  group=128 uses group-wise scales; keep_dense=False
     drops the dense copy; device places the buffers (default: the weight's CUDA
-    device, else the current one)."""
+    device, else the current one).  quantizer="gpu" quantises and packs each weight in
+    one kernel launch on the target GPU (bit-identical codes and fp32 scales) instead of
+    the reference's torch ops."""
+    if quantizer not in ("torch", "gpu"):
+        raise ValueError("quantizer must be 'torch' or 'gpu'")
     for name, child in module.named_children():
         if isinstance(child, nn.Linear):
             w = child.weight.data
@@ -75,14 +79,21 @@ def replace_linear_with_w4a16(module, group=0, keep_dense=True, scale_dtype=torc
                 dev = torch.device(device)
             else:
                 dev = w.device if w.is_cuda else torch.device("cuda", torch.cuda.current_device())
-            if group:
-                q, scale = quantize_int4_group(w.float(), group=group)
+            if quantizer == "gpu":
+                if dev.type != "cuda":
+                    raise ValueError("quantizer='gpu' needs a CUDA device")
+                packed, scale = K.quantize_pack(w.to(dev).float().contiguous(), group=group,
+                                                scale_dtype=scale_dtype)
             else:
-                q, scale = quantize_int4_symmetric(w.float())
-            packed = pack_int4_interleaved(q).to(dev)
+                if group:
+                    q, scale = quantize_int4_group(w.float(), group=group)
+                else:
+                    q, scale = quantize_int4_symmetric(w.float())
+                packed = pack_int4_interleaved(q).to(dev)
+                scale = scale.to(scale_dtype).to(dev)
             dense = w.half().to(dev) if keep_dense else None
-            setattr(module, name, W4A16Linear(dense, child.bias, packed, scale.to(scale_dtype).to(dev)))
+            setattr(module, name, W4A16Linear(dense, child.bias, packed, scale))
         else:
             replace_linear_with_w4a16(child, group=group, keep_dense=keep_dense,
-                                      scale_dtype=scale_dtype, device=device)
+                                      scale_dtype=scale_dtype, device=device, quantizer=quantizer)
     return module
