@@ -79,3 +79,23 @@ def test_rejects_mismatches(tmp_path):
     torch.save({"format": "other"}, tmp_path / "bad.pt")
     with pytest.raises(ValueError, match="checkpoint"):
         K.load_quantized(_toy(3), tmp_path / "bad.pt", device="cpu")
+
+
+@pytest.mark.gpu
+def test_loaded_model_gives_the_same_logits_on_gpu(tmp_path):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=64, vocab_size=1024, tie_word_embeddings=True)
+    torch.manual_seed(0)
+    src = LlamaForCausalLM(cfg).half().cuda().eval()
+    K.replace_linear_with_w4a16(src, group=128, keep_dense=False, quantizer="gpu")
+    path = tmp_path / "llama.pt"
+    K.save_quantized(src, path)
+    torch.manual_seed(1)
+    dst = K.load_quantized(LlamaForCausalLM(cfg).half().cuda().eval(), path)
+    ids = torch.tensor([[3, 14, 15, 92]], device="cuda")
+    with torch.no_grad():
+        la = src(ids, use_cache=False).logits
+        lb = dst(ids, use_cache=False).logits
+    assert torch.isfinite(la).all() and torch.equal(la, lb)
