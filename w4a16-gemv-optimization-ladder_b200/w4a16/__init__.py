@@ -25,6 +25,7 @@ from .kernels import (
     w4a16_gemv,
     w4a16_gemv_g128,
 )
+from . import ops  # noqa: F401  (registers torch.ops.w4a16.*)
 from .checkpoint import load_quantized, save_quantized
 from .linear import W4A16Linear, replace_linear_with_w4a16
 from .quant import (
