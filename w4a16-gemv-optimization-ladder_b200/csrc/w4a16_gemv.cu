@@ -4,18 +4,26 @@
 // that TMA (cp.async.bulk.tensor, 128-byte swizzle) fills with 16-row x 1024-column
 // windows of packed int4 weights (one 3-D box per window) and, for group-128, the
 // matching scale tile.  The warp decodes each packed word to f16x2 codes in
-// registers (decode_word: shift + 4 lop3 + 4 f16x2 ops, exact) and feeds them as the
-// A operand of mma.sync.m16n8k16 with the activation as the B operand, so products
-// are exact and accumulation is fp32 in the tensor core.  Columns of B carry up to
-// 8 (16 with two MMAs) activation rows: batch 1..16 costs the same weight traffic
-// as batch 1.  Group-128 partial sums are scaled in fp32 once per group; per-row
-// sums once per row.
+// registers (exact) and feeds them as the A operand of mma.sync.m16n8k16 with the
+// activation as the B operand, so products are exact and accumulation is fp32 in the
+// tensor core.  Columns of B carry up to 8 (16 with two MMAs) activation rows: batch
+// 1..16 costs the same weight traffic as batch 1.  For one activation vector the
+// decode leaves half of the nibbles biased by +72 (decode_word_fold, 7 instructions
+// per word) and every 128-column group starts its accumulator at -72 * (sum of the
+// activation over those columns); group-128 sums are scaled once per group in fp32,
+// per-row sums once per row.
 //
-// Scheduling is stream-K over (tile, 256-column slab) units: a persistent grid of
-// one CTA per SM gives every warp an equal contiguous range of units, so all warps
-// finish together whatever the shape.  A tile split between neighbouring warps is
-// finished by the last of them, which adds the published partial sums in warp
-// order (deterministic).  Without a workspace each warp owns whole tiles instead.
+// One activation vector is staged in shared memory by the CTA, optionally computed
+// on the way (RMSNorm of an fp32 vector, or SwiGLU of a gate|up vector: the decode
+// step's prologues).  Launches may be chained (programmatic dependent launch): the
+// weight copies start before the wait for the previous kernel.
+//
+// Work is split over (16-row tile, 1024-column window) units with a persistent grid
+// of one CTA per SM: dynamic whole-tile pulls, stream-K ranges finished by the last
+// contributor (partials added in warp order, deterministic), static whole tiles, or
+// CTA-local ranges reduced in shared memory for small matrices (see Sched).  The
+// fused all-gather (TP kernels only) writes each output row into every rank's buffer
+// over NVLink and signals completion through flags in those buffers.
 //
 // Reference counterparts: k_marlin (kernels/w4a16_kernels.cu:100-114) and
 // k_marlin_g128 (:121-138) compute the same sums with one warp per row, 4-byte
