@@ -79,3 +79,21 @@ def test_chained_launches_change_nothing():
         outs.append(dec.replay(token=9, pos=70).clone())
     torch.cuda.synchronize()
     assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
+def test_greedy_generation_on_device_matches_eager_loop():
+    from w4a16.decode import W4A16LlamaDecoder
+
+    dec = W4A16LlamaDecoder(_small(), seed=7)
+    dec.fill_cache(20)
+    k0, v0 = dec.k_cache.clone(), dec.v_cache.clone()
+    toks = dec.generate(token=11, pos=20, n=12)            # graph replays, argmax fed back on device
+    dec.k_cache.copy_(k0)
+    dec.v_cache.copy_(v0)
+    want, t = [], 11
+    for i in range(12):                                      # the same steps launched one by one
+        t = int(dec.step(token=t, pos=20 + i).argmax())
+        want.append(t)
+    assert toks.tolist() == want
+    with pytest.raises(ValueError):
+        dec.generate(token=1, pos=120, n=20)

@@ -137,6 +137,11 @@ class W4A16LlamaDecoder:
         self.ws = [K.new_workspace(dev), K.new_workspace(dev)] if self.fused else None
         self.logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
         self.graph = None
+        # greedy generation on the device: the next token and position are written by the
+        # graph itself, generated tokens collected in gen_tokens
+        self.gen_tokens = torch.zeros(cfg.max_len, dtype=torch.long, device=dev)
+        self.gen_idx = torch.zeros(1, dtype=torch.long, device=dev)
+        self.gen_graph = None
 
     # ------------------------------------------------------------------ pieces
 
@@ -239,6 +244,49 @@ class W4A16LlamaDecoder:
             self._step()
         return self.graph
 
+    def _greedy_step(self):
+        logits = self._step()
+        nxt = torch.argmax(logits).view(1)
+        self.gen_tokens.index_copy_(0, self.gen_idx, nxt)
+        self.token.copy_(nxt)
+        self.pos.add_(1)
+        self.gen_idx.add_(1)
+
+    def capture_generate(self):
+        """Record one greedy step in a CUDA graph: the step, the argmax of the logits fed
+        back as the next token, the position advanced; replays need no host round trip."""
+        K.reserve_workspace(self.device, 1, self.cfg.vocab, self.cfg.hidden)
+        saved = (self.token.clone(), self.pos.clone(), self.gen_idx.clone(), self.k_cache.clone(),
+                 self.v_cache.clone())
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside capture (restored below)
+                self.pos.zero_()
+                self.gen_idx.zero_()
+                self._greedy_step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        self.gen_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.gen_graph):
+            self._greedy_step()
+        for t, v in zip((self.token, self.pos, self.gen_idx, self.k_cache, self.v_cache), saved):
+            t.copy_(v)
+        return self.gen_graph
+
+    def generate(self, token, pos, n):
+        """Greedy continuation of `token` at position `pos` for n tokens (graph replays);
+        returns the n generated token ids on the host."""
+        if pos + n > self.cfg.max_len:
+            raise ValueError(f"pos + n = {pos + n} exceeds the cache length {self.cfg.max_len}")
+        if self.gen_graph is None:
+            self.capture_generate()
+        self.token.fill_(int(token))
+        self.pos.fill_(int(pos))
+        self.gen_idx.zero_()
+        for _ in range(n):
+            self.gen_graph.replay()
+        return self.gen_tokens[:n].cpu()
+
     def replay(self, token, pos):
         """Graph step: set token/pos on the device, replay, return the logits buffer."""
         self.token.fill_(int(token))
@@ -297,6 +345,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch op by op (no CUDA graph)")
+    ap.add_argument("--generate", type=int, default=0,
+                    help="also generate this many tokens greedily on the device and report tokens/s")
     a = ap.parse_args(argv)
     cfg = LlamaDecodeConfig(layers=a.layers, max_len=a.max_len)
     dec = W4A16LlamaDecoder(cfg, dense=a.mode == "dense", fused=a.mode == "fused",
@@ -320,9 +370,21 @@ def main(argv=None):
     en.record()
     torch.cuda.synchronize()
     us = st.elapsed_time(en) * 1000.0 / max(a.steps, 1)
-    print(json.dumps({"mode": a.mode, "pdl": dec.pdl, "graph": not a.eager, "layers": cfg.layers,
-                      "kv_len": pos + 1, "step_us": round(us, 2), "weight_bytes": dec.weight_bytes(),
-                      "weight_gbs": round(dec.weight_bytes() / us / 1e3, 1)}))
+    res = {"mode": a.mode, "pdl": dec.pdl, "graph": not a.eager, "layers": cfg.layers,
+           "kv_len": pos + 1, "step_us": round(us, 2), "weight_bytes": dec.weight_bytes(),
+           "weight_gbs": round(dec.weight_bytes() / us / 1e3, 1)}
+    if a.generate:
+        n = min(a.generate, cfg.max_len - 1)
+        dec.capture_generate()
+        dec.generate(1, 0, 4)  # warm
+        torch.cuda.synchronize()
+        st.record()
+        toks = dec.generate(1, 0, n)
+        en.record()
+        torch.cuda.synchronize()
+        res.update({"generated": n, "tokens_per_s": round(n / (st.elapsed_time(en) / 1000.0), 1),
+                    "first_tokens": toks[:8].tolist()})
+    print(json.dumps(res))
 
 
 if __name__ == "__main__":
