@@ -364,6 +364,11 @@ def run_ours(args, rank, world, dev):
         extras["per_row_us"] = round(row_us, 3)
         extras["per_row_frac_of_peak"] = round(rbytes / (row_us * 1e-6) / 1e9 / peak, 4)
         extras["g128_frac_of_peak"] = result["roofline"]["frac"]
+        # the reference's own numbers for this shape (A100-SXM4-40GB, README.md:38; other
+        # hardware, so context only: vs_baseline stays null)
+        extras["reference_a100_us"] = {"g128": 247.1, "per_row": 214.2}
+        extras["speedup_vs_reference_a100"] = {"g128": round(247.1 / kernel_us, 2),
+                                               "per_row": round(214.2 / row_us, 2)}
         # the same launches without chaining (each kernel starts after the previous ends)
         extras["g128_unchained_us"] = round(g128_plain_us, 3)
         extras["g128_unchained_frac_of_peak"] = round(nbytes / (g128_plain_us * 1e-6) / 1e9 / peak, 4)
