@@ -20,6 +20,7 @@ over ranks) / N, i.e. µs per 262144x2048 GEMV-equivalent of the whole job.
 src/w4a16/kernels.py:98-101) as restated by the C oracle, on all host threads.
 """
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -193,24 +194,33 @@ def ncu_traffic(name):
     return None
 
 
-def cpu_baseline(packed, scale, x, group, budget_s=10.0):
-    """The C oracle (fp32 dequant + fp32 dot, all host threads) on the full matrix,
-    repeated until `budget_s` of CPU time; returns (µs per GEMV, threads, reps)."""
+def time_c_reference(packed, scale, x, group, steps, warmup, threads):
+    """The C restatement of the reference's CPU path (fp32 dequant then fp32 dot per row,
+    pthreads over rows) on numpy inputs: `warmup` untimed calls, then `steps` calls timed
+    one by one; returns the median µs per call (the host's cores are shared, so single
+    calls can be slowed by other work on the machine)."""
     from oracle import c_oracle
+
     c_oracle.build()
-    p = packed.cpu().numpy()
-    s = scale.cpu().numpy()
-    xv = x.cpu().numpy()
+    for _ in range(warmup):
+        c_oracle.gemv(packed, scale, x, group=group, accumulate_f64=False, threads=threads)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        c_oracle.gemv(packed, scale, x, group=group, accumulate_f64=False, threads=threads)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e6
+
+
+def cpu_baseline(packed, scale, x, group, steps=20, warmup=5):
+    """The same timing as the reference arm (time_c_reference) on this arm's weights;
+    returns (µs per GEMV, threads, calls)."""
+    from oracle import c_oracle
+
     threads = c_oracle.max_threads()
-    c_oracle.gemv(p, s, xv, group=group, accumulate_f64=False, threads=threads)
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        c_oracle.gemv(p, s, xv, group=group, accumulate_f64=False, threads=threads)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s or reps >= 50:
-            break
-    return el / reps * 1e6, threads, reps
+    us = time_c_reference(packed.cpu().numpy(), scale.cpu().numpy(), x.cpu().numpy(), group, steps,
+                          warmup, threads)
+    return us, threads, steps
 
 
 # -------------------------------------------------------------------- arms
@@ -342,7 +352,12 @@ def run_ours(args, rank, world, dev):
 
     extras = {}
     if tp_choice is not None:
+        tp_choice["gemv_alone_us"] = round(kernel_us, 3)
+        tp_choice["overhead_us"] = {k[:-8]: round(tp_choice[k] - kernel_us, 3)
+                                    for k in ("fused_step_us", "nccl_step_us")}
         extras["tensor_parallel"] = tp_choice
+    if not args.no_llama8b:
+        extras["llama8b"] = llama8b_times(K, rank, world, dev, stream, load_peaks()[0])
     if rank == 0:
         # per-row variant of the same shape
         prow = [make_weights(ROWS, COLS, 0, seed=50 + c, device=dev) for c in range(2)]
@@ -462,27 +477,167 @@ def run_ours(args, rank, world, dev):
                      "api": ("w4a16.tp.FusedAllGatherW4A16 (C ABI w4a16_gemv_allgather)" if world > 1
                              else "w4a16.w4a16_gemv_g128 (C ABI w4a16_gemv)")}
 
-    # correctness of the benchmarked kernel on this data, against the oracle (rank 0)
+    # correctness of what was benchmarked, against the oracle: the device error word after
+    # the timed steps (a bounded wait that gave up), then one more step of each timed path
+    # on weight copy 0 compared with the oracle over every row the step produces (at N > 1
+    # the whole gathered (N*262144)-row output on every rank, fused and NCCL)
+    result["check"] = verify_outputs(K, copies[0], x, y, gemv_fn, wss, tpa, rank, world, dev)
     if rank == 0:
-        from oracle import c_oracle
-        yk = K.w4a16_gemv_g128(copies[0][0], copies[0][1], x).cpu().numpy()
-        ref = c_oracle.gemv(copies[0][0].cpu().numpy(), copies[0][1].cpu().numpy(), x.cpu().numpy(),
-                            group=GROUP)
-        import numpy as np
-        err = np.abs(yk - ref)
-        extras["max_abs_err_vs_oracle"] = float(err.max())
-        extras["within_tolerance"] = bool((err <= 1e-3 + 1e-3 * np.abs(ref)).all())
         if world == 1 and not args.no_cpu_baseline:
             us, threads, reps = cpu_baseline(copies[0][0], copies[0][1], x, GROUP)
             result["cpu_baseline"] = {"value": round(us, 1), "unit": "µs", "cores": threads,
                                       "kind": "port",
-                                      "sample": f"full 262144x2048 g128 GEMV, {reps} repetitions "
-                                                "(C oracle: fp32 dequant then fp32 dot, pthreads)"}
+                                      "sample": f"full 262144x2048 g128 GEMV, median of {reps} calls after "
+                                                "5 warm-up (C restatement of kernels.py:98-101: fp32 "
+                                                "dequant then fp32 dot, pthreads)"}
     result["clocks"] = sampler.summary() if sampler else None
     result["extras"] = extras
     if tpa is not None:
         tpa.close()
     return result
+
+
+def verify_outputs(K, copy, x, y, gemv_fn, wss, tpa, rank, world, dev):
+    """Device error word after the timed steps, then the outputs of one more step of each
+    timed path against the oracle.  Every rank computes the oracle for its own shard (the
+    C oracle, float64 sums) and the shards are all-gathered, so each rank compares its whole
+    gathered output.  Returns max error, tolerance verdict and error code (max over ranks)."""
+    import numpy as np
+    from oracle import c_oracle
+
+    code = K.read_device_error(dev)  # synchronises: the timed steps are done
+    packed, scale = copy
+    threads = max(1, c_oracle.max_threads() // max(1, world))
+    ref_local = c_oracle.gemv(packed.cpu().numpy(), scale.cpu().numpy(), x.cpu().numpy(), group=GROUP,
+                              threads=threads)
+    ref = torch.from_numpy(ref_local).to(dev)
+    if world > 1:
+        full = torch.empty(world * ROWS, dtype=torch.float32, device=dev)
+        torch.distributed.all_gather_into_tensor(full, ref)
+        ref = full
+    outs = {}
+    if world == 1:
+        gemv_fn(packed, scale, y, GROUP, wss[0], chained=True)()   # the timed entry
+        outs["gemv_fused_entry"] = y.clone()
+        outs["w4a16_gemv_g128"] = K.w4a16_gemv_g128(packed, scale, x)  # the public op
+    else:
+        torch.distributed.barrier()  # every rank's oracle is done before the peer waits start
+        outs["fused"] = tpa.launch(packed, scale, x).clone()
+        gathered = torch.empty(world * ROWS, dtype=torch.float32, device=dev)
+        gemv_fn(packed, scale, y, GROUP, wss[0], chained=False)()
+        torch.distributed.all_gather_into_tensor(gathered, y)
+        outs["nccl"] = gathered
+    torch.cuda.synchronize()
+    code = max(code, K.read_device_error(dev))
+    refn = ref.cpu().numpy().astype(np.float64)
+    worst, ok = 0.0, True
+    per_path = {}
+    for name, out in outs.items():
+        err = np.abs(out.cpu().numpy().astype(np.float64) - refn)
+        per_path[name] = float(err.max())
+        worst = max(worst, float(err.max()))
+        ok &= bool((err <= 1e-3 + 1e-3 * np.abs(refn)).all())
+    stats = torch.tensor([worst, 0.0 if ok else 1.0, float(code)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+    return {"max_abs_err_vs_oracle": float(stats[0]), "within_tolerance": bool(stats[1] == 0.0),
+            "device_error": int(stats[2]), "rows_checked": int(ref.numel()), "paths": per_path,
+            "tolerance": "|y - oracle| <= 1e-3 + 1e-3 |oracle| for every row"}
+
+
+# Llama-3-8B-shaped projections (hidden 4096, MLP 14336, GQA 32/8 heads of 128, vocab
+# 128256), group-128 int4: q, k (= v), gate (= up), down and the head.
+LLAMA8B_SHAPES = (("q_proj", 4096, 4096), ("kv_proj", 1024, 4096), ("gate_up", 14336, 4096),
+                  ("down_proj", 4096, 14336), ("lm_head", 128256, 4096))
+LLAMA8B_BATCHES = (1, 4, 16)
+ROTATE_BYTES = 300 << 20  # weight copies cycled per timed loop: > 2x the 126 MB L2
+
+
+def llama8b_times(K, rank, world, dev, stream, peak, reps=200):
+    """Every Llama-3-8B-shaped layer at batch 1, 4 and 16, row-sharded over the running
+    N GPUs: per shape and batch the step time (max over ranks) of the local GEMV plus,
+    at N > 1, the NCCL all-gather that assembles [batch, rows] on every rank (and, at
+    batch 1, the GEMV with the all-gather fused into its epilogue), the GEMV alone, and
+    the per-GPU weight bytes / step time against the HBM peak.  Each timed loop cycles
+    through enough weight copies (random codes, positive scales) to exceed 2x the L2."""
+    from w4a16.tp import FusedAllGatherW4A16, shard_bounds
+
+    out = {}
+    for name, rows, cols in LLAMA8B_SHAPES:
+        lo, hi = shard_bounds(rows, world, rank)
+        n = hi - lo
+        chunk = shard_bounds(rows, world, 0)[1]
+        pbytes, sbytes = n * cols // 2, n * (cols // GROUP) * 4
+        ncopy = max(2, -(-ROTATE_BYTES // (pbytes + sbytes)))
+        g = torch.Generator(device=dev).manual_seed(100 + rows + cols + rank)
+        pbuf = torch.randint(0, 256, (ncopy * pbytes,), dtype=torch.uint8, device=dev, generator=g)
+        sbuf = torch.rand(ncopy * n * (cols // GROUP), device=dev, generator=g) * 2e-3 + 2e-3
+        copies = [(pbuf[c * pbytes:(c + 1) * pbytes].view(n, cols // 2),
+                   sbuf[c * n * (cols // GROUP):(c + 1) * n * (cols // GROUP)].view(n, cols // GROUP))
+                  for c in range(ncopy)]
+        fused = None
+        if world > 1:
+            fused = FusedAllGatherW4A16(copies[0][0], copies[0][1], rows, group=GROUP)
+        res = {"rows": rows, "cols": cols, "rows_per_gpu": n, "weight_bytes_per_gpu": pbytes + sbytes,
+               "weight_copies": ncopy}
+        for b in LLAMA8B_BATCHES:
+            x = torch.randn(b, cols, device=dev, generator=g).half()
+            local = torch.empty(b, chunk, dtype=torch.float32, device=dev)
+            gathered = torch.empty(world, b, chunk, dtype=torch.float32, device=dev)
+            full = torch.empty(b, rows, dtype=torch.float32, device=dev)
+
+            def gemv(c, b=b, x=x, local=local):
+                pc, sc = copies[c]
+                K.gemv(pc, sc, x if b > 1 else x[0], group=GROUP,
+                       out=local[:, :n] if b > 1 else local[0, :n])
+
+            def step(c, b=b, local=local, gathered=gathered, full=full):
+                gemv(c)
+                if world > 1:
+                    torch.distributed.all_gather_into_tensor(gathered.view(-1), local.view(-1))
+                    if b > 1:  # [world, batch, rows/world] -> [batch, rows]
+                        full.view(b, world, chunk).copy_(gathered.permute(1, 0, 2))
+
+            def loop_us(fn):
+                """One graph launching every copy once, replayed; µs per launch."""
+                for c in range(2):
+                    fn(c)
+                torch.cuda.synchronize()
+                graph = capture_steps([lambda c=c: fn(c) for c in range(ncopy)])
+                replays = max(1, reps // ncopy)
+                graph.replay()
+                torch.cuda.synchronize()
+                if world > 1:
+                    torch.distributed.barrier()
+                ms = time_graphs([graph, None], [1, 0], replays, stream)
+                del graph
+                t = torch.tensor([ms], device=dev)
+                if world > 1:
+                    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                return t.item() * 1000.0 / (replays * ncopy)
+
+            r = {"gemv_us": round(loop_us(gemv), 3)}
+            if world > 1:
+                r["nccl_step_us"] = round(loop_us(step), 3)
+                if b == 1:
+                    r["fused_step_us"] = round(loop_us(
+                        lambda c: fused.launch(copies[c][0], copies[c][1], x[0],
+                                               stream=ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                               pdl=True)), 3)
+                    if fused.device_error():
+                        raise RuntimeError(f"llama8b {name}: the fused all-gather reported a timed-out wait")
+            step_us = min(v for k, v in r.items() if k.endswith("step_us")) if world > 1 else r["gemv_us"]
+            r["step_us"] = step_us
+            r["gbs_per_gpu"] = round((pbytes + sbytes) / (step_us * 1e-6) / 1e9, 1)
+            r["frac_of_peak"] = round(r["gbs_per_gpu"] / peak, 4)
+            r["gemv_frac_of_peak"] = round((pbytes + sbytes) / (r["gemv_us"] * 1e-6) / 1e9 / peak, 4)
+            res[f"batch{b}"] = r
+        if fused is not None:
+            fused.close()
+        out[name] = res
+        del copies, pbuf, sbuf
+        torch.cuda.empty_cache()
+    return out
 
 
 def decode_step_times(dev, stream, reps=200):
@@ -522,45 +677,87 @@ def decode_step_times(dev, stream, reps=200):
     return out
 
 
-def run_reference(args, rank, world):
-    """The reference's CPU algorithm (dequant then matmul, fp32) via the C oracle on
-    a bounded row sample of the same workload, extrapolated to the full matrix."""
-    from oracle import c_oracle
+def reference_inputs():
+    """The benchmark's group-128 262144x2048 workload as the GPU arm builds it: the same
+    seeded fp16 weights (torch's CUDA generator, seed 0, as rank 0's first weight copy)
+    and activation (seed 7), quantised and packed on the host by the C oracle, whose
+    codes and scales equal the reference's quantize_int4_group + pack_int4_interleaved
+    (kernels.py:52-60, :73-91).  No kernel of this library runs here."""
     import numpy as np
+    from oracle import c_oracle
+
+    if torch.cuda.is_available():
+        dev = torch.device("cuda", 0)
+        g = torch.Generator(device=dev).manual_seed(0)
+        w = (torch.randn(ROWS, COLS, device=dev, generator=g) * 0.02).half().cpu()
+        gx = torch.Generator(device=dev).manual_seed(7)
+        x = torch.randn(COLS, device=dev, generator=gx).half().cpu()
+        same = True
+    else:  # no GPU here: the same distributions from the CPU generator
+        g = torch.Generator().manual_seed(0)
+        w = (torch.randn(ROWS, COLS, generator=g) * 0.02).half()
+        x = torch.randn(COLS, generator=g).half()
+        same = False
+    packed, scale = c_oracle.quantize_pack(w.float().numpy(), group=GROUP)
+    return packed, scale, x.numpy().astype(np.float16), same
+
+
+def time_reference_torch(packed, scale, x, threads, budget_s=30.0):
+    """The reference's own CPU expression for this path, dequant_ref_group
+    (src/w4a16/kernels.py:98-101): (q.float() * scale.repeat_interleave(128, 1)) @ x.float(),
+    restated with the same torch ops on the codes unpacked from `packed`.  One untimed
+    call, then as many timed calls (1..3) as fit in `budget_s`; µs per call."""
+    from oracle import w4a16_oracle as O
+
+    torch.set_num_threads(threads)
+    q = torch.from_numpy(O.unpack_int4(packed))
+    s = torch.from_numpy(scale)
+    v = torch.from_numpy(x)
+
+    def call():
+        scale_full = s.repeat_interleave(GROUP, dim=1)
+        return (q.float() * scale_full) @ v.float()
+
+    t0 = time.perf_counter()
+    call()
+    first = time.perf_counter() - t0
+    n = max(1, min(3, int(budget_s / max(first, 1e-3)) - 1))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        call()
+    return (time.perf_counter() - t0) / n * 1e6, n
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU path (dequant then matmul in fp32, kernels.py:98-101) on the
+    full group-128 262144x2048 workload of the GPU arm, on all host threads: the C
+    restatement (fused dequant + fp32 dot per row, pthreads) is the timed step; the
+    reference's literal torch expression is timed beside it (reference_torch)."""
+    from oracle import c_oracle
 
     c_oracle.build()
     threads = c_oracle.max_threads()
-    rng = np.random.default_rng(0)
-    probe_rows = 4096
-    w = (rng.standard_normal((probe_rows, COLS), dtype=np.float32) * 0.02).astype(np.float16)
-    packed, scale = c_oracle.quantize_pack(w.astype(np.float32), group=GROUP)
-    x = rng.standard_normal(COLS).astype(np.float16)
-    t0 = time.perf_counter()
-    c_oracle.gemv(packed, scale, x, group=GROUP, accumulate_f64=False, threads=threads)
-    per_row = (time.perf_counter() - t0) / probe_rows
-    budget = 120.0  # seconds for warmup + steps
-    rows = int(budget / max(1, args.steps + args.warmup) / max(per_row, 1e-9))
-    rows = max(128, min(probe_rows, rows // 16 * 16))
-    p, s = packed[:rows], scale[:rows]
-    for _ in range(args.warmup):
-        c_oracle.gemv(p, s, x, group=GROUP, accumulate_f64=False, threads=threads)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        c_oracle.gemv(p, s, x, group=GROUP, accumulate_f64=False, threads=threads)
-    el = time.perf_counter() - t0
-    us_full = el / args.steps * 1e6 * (ROWS / rows)
-    sample = (f"{rows} of 262144 rows x 2048 per step (g128), extrapolated x{ROWS / rows:.0f} "
-              "to the full matrix; C oracle restating kernels.py:98-101")
-    return {"impl": "reference", "metric": METRIC, "value": round(us_full, 1), "unit": "µs",
+    packed, scale, x, same = reference_inputs()
+    us = time_c_reference(packed, scale, x, GROUP, args.steps, args.warmup, threads)
+    torch_us, torch_n = time_reference_torch(packed, scale, x, threads)
+    sample = (f"full 262144x2048 g128 GEMV per step, median of {args.steps} timed steps after "
+              f"{args.warmup} warm-up; C restatement of kernels.py:98-101: fp32 dequant then fp32 dot, "
+              "pthreads")
+    return {"impl": "reference", "metric": METRIC, "value": round(us, 1), "unit": "µs",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(us_full / 1000.0, 3), "higher_is_better": False,
+            "ms_per_step": round(us / 1000.0, 3), "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "g128 int4 GEMV 262144x2048, batch 1", "rows_per_gpu": ROWS,
                        "cols": COLS, "group": GROUP,
-                       "parallelism": "host cores of rank 0 (the reference's CPU path)"},
-            "cpu_baseline": {"value": round(us_full, 1), "unit": "µs", "cores": threads,
+                       "parallelism": "host cores of rank 0 (the reference's CPU path)",
+                       "same_inputs_as_gpu_arm": same},
+            "cpu_baseline": {"value": round(us, 1), "unit": "µs", "cores": threads,
                              "kind": "port", "sample": sample},
-            "e2e": {"value": round(us_full, 1), "unit": "µs", "h2d_bytes_per_step": 0,
+            "reference_torch": {"value": round(torch_us, 1), "unit": "µs", "cores": threads,
+                                "calls": torch_n,
+                                "expr": "(q.float() * scale.repeat_interleave(128, dim=1)) @ vec.float() "
+                                        "(dequant_ref_group, kernels.py:98-101, same torch ops)"},
+            "e2e": {"value": round(us, 1), "unit": "µs", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
 
@@ -572,6 +769,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step measurement")
+    ap.add_argument("--no-llama8b", action="store_true",
+                    help="skip the Llama-3-8B-shaped layers (batch 1/4/16, row-sharded over N GPUs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -628,9 +827,15 @@ def main():
         "e2e": res["e2e"],
         "gpu_launches": args.steps,
         "clocks": res["clocks"],
+        "within_tolerance": res["check"]["within_tolerance"],
+        "device_error": res["check"]["device_error"],
+        "check": res["check"],
         "extras": res["extras"],
     }
     print(json.dumps(line), flush=True)
+    if not res["check"]["within_tolerance"] or res["check"]["device_error"]:
+        sys.exit(f"bench: outputs failed the oracle check or a kernel reported error "
+                 f"{res['check']['device_error']}")
 
 
 if __name__ == "__main__":

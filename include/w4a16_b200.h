@@ -121,7 +121,9 @@ int w4a16_fp16_cuda(const void* mat, const void* vec, float* out, int rows, int 
  *              reduced through it); without it each warp owns whole 16-row tiles.
  *              The kernels leave its counter block zeroed, so zero-filling once is
  *              enough (the partial sums are scratch).  Calls that share a workspace must be
- *              ordered on one stream. */
+ *              ordered on one stream.  Exception: after w4a16_read_device_error reports a
+ *              non-zero code, a warp may have returned early and left counters behind:
+ *              zero-fill again every workspace used since the previous read. */
 int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_dtype, int group,
                const void* x, int batch, int rows, int cols, void* out, int out_dtype,
                const float* bias, void* workspace, size_t workspace_bytes,
@@ -189,15 +191,26 @@ int w4a16_tp_region_close(void* region, int owned);
  * announced it (so no rank overwrites a buffer a peer is still reading from the previous
  * step); the kernel's last CTA publishes this rank's completion and waits for every rank's,
  * so when the call completes on the stream the gathered output is whole on this rank.
- * Waits are bounded (2 s): a missing peer sets the device error word
- * (w4a16_read_device_error, code 2) and the step then writes this rank's own rows only.
- * regions: host array of nranks device pointers (own region at index rank).  Stream-ordered
- * and graph-capturable: step numbers live in the regions.  flags: 0 or W4A16_LAUNCH_PDL
- * (then consecutive calls must alternate two workspaces, as for w4a16_gemv_fused). */
+ * Waits are bounded (2 s by default, w4a16_tp_set_peer_wait_ns): a missing peer sets the
+ * device error word (w4a16_read_device_error, code 2) and the step then writes this rank's
+ * own rows only; the ranks' step numbers no longer agree after that, so close the regions
+ * and allocate new ones before the next step.
+ * regions: host array of nranks device pointers (own region at index rank), each returned by
+ * w4a16_tp_region_alloc or w4a16_tp_region_open in this process; rows [row0, row0 + rows) must
+ * fit the gathered output of every region (out_bytes given to w4a16_tp_region_alloc), else
+ * W4A16_ERR_SHAPE with nothing launched.  Stream-ordered and graph-capturable: step numbers
+ * live in the regions.  flags: 0 or W4A16_LAUNCH_PDL (then consecutive calls must alternate
+ * two workspaces, as for w4a16_gemv_fused). */
 int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dtype, int group,
                          const void* x, int rows, int cols, int out_dtype, long long row0, int rank,
                          int nranks, void* const* regions, void* workspace, size_t workspace_bytes,
                          unsigned flags, w4a16_stream_t stream);
+
+/* Limit, in nanoseconds, of each wait of w4a16_gemv_allgather on another rank's flags,
+ * for the calls made after this one in the process (0 restores the 2 s default; otherwise
+ * 1 us .. 60 s, else W4A16_ERR_SHAPE).  A short limit lets a caller that must detect a
+ * missing rank quickly (a failure-detection test, a watchdog) get the error code sooner. */
+int w4a16_tp_set_peer_wait_ns(unsigned long long ns);
 
 /* Bytes of workspace that let w4a16_gemv balance its work across warps (stream-K)
  * for this batch size; independent of rows and cols (about 0.5 MiB per activation
@@ -212,8 +225,9 @@ size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols);
  * so nothing is allocated.  The scratch a call needs (w4a16_gemv_workspace_bytes(1,
  * rows, cols), about 0.5 MiB) does not grow with the matrix; a call needing more than
  * 4 MiB would get W4A16_ERR_WORKSPACE with nothing run.  The first call on a device looks up the
- * array's address; make it before any stream capture.  All calls share the array:
- * calls that overlap on the GPU race, so order them on one stream. */
+ * array's address (again after the device's current context changes); make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU race, so order
+ * them on one stream. */
 int w4a16_gemv_noalloc(const uint8_t* packed, const void* scale, int scale_dtype, int group,
                        const void* x, int rows, int cols, float* out, w4a16_stream_t stream);
 
@@ -234,7 +248,11 @@ int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int grou
                         uint8_t* packed, void* scale, int scale_dtype, w4a16_stream_t stream);
 
 /* Reads and clears the error word that kernels set when a bounded wait runs out
- * (0 = none).  Synchronises `stream`. */
+ * (0 = none; 1 = a weight copy did not land in time; 2 = another rank's flag did not
+ * arrive in time).  Synchronises `stream`.  A non-zero code means some warps returned
+ * early: their rows of the output are missing, and a split-K workspace they used may hold
+ * non-zero counters, so zero-fill again every workspace used since the previous read
+ * (w4a16_gemv_noalloc clears its own on every call). */
 int w4a16_read_device_error(int* code, w4a16_stream_t stream);
 
 /* Static text for a status code. */

@@ -49,7 +49,16 @@ int main(void) {
     expect(w4a16_gemv_allgather(packed, scale, W4A16_DTYPE_F32, 0, x, 16, 256, W4A16_DTYPE_F32, 0, 2, 2,
                                 regions, NULL, 0, 0u, NULL) == W4A16_ERR_SHAPE,
            "allgather rank out of range rejected");
+    /* regions this process neither allocated nor opened are rejected before any launch */
+    expect(w4a16_gemv_allgather(packed, scale, W4A16_DTYPE_F32, 0, x, 16, 256, W4A16_DTYPE_F32, 0, 0, 2,
+                                regions, NULL, 0, 0u, NULL) == W4A16_ERR_SHAPE,
+           "allgather into unknown regions rejected");
+    expect(strstr(w4a16_last_error_string(), "w4a16_tp_region_alloc") != NULL,
+           "unknown region error names the allocator");
   }
+  expect(w4a16_tp_set_peer_wait_ns(1ull) == W4A16_ERR_SHAPE, "1 ns peer wait rejected");
+  expect(w4a16_tp_set_peer_wait_ns(100000000ull) == W4A16_OK, "100 ms peer wait accepted");
+  expect(w4a16_tp_set_peer_wait_ns(0ull) == W4A16_OK, "peer wait default restored");
   if (failures == 0) printf("c abi ok\n");
   return failures == 0 ? 0 : 1;
 }

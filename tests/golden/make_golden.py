@@ -4,10 +4,11 @@ Runs the REFERENCE's own Python functions (src/w4a16/kernels.py of
 emirabayer/w4a16-gemv-optimization-ladder: quantize_int4_symmetric,
 quantize_int4_group, pack_int4, pack_int4_interleaved, dequant_ref,
 dequant_ref_group, and benchmarks/perplexity.py's per-row fake-quant formula) on CPU
-over small seeded inputs and stores inputs and outputs.  Run it where the reference
-checkout is available; the tests only read the .npz.
+over small seeded inputs and stores inputs and outputs.  Run it where a checkout of
+the reference is available, naming that checkout; the tests only read the .npz.
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
+    W4A16_REFERENCE=/path/to/reference python tests/golden/make_golden.py
 """
 import os
 import sys
@@ -15,7 +16,9 @@ import sys
 import numpy as np
 import torch
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("W4A16_REFERENCE")
+if not REF:
+    sys.exit("usage: make_golden.py /path/to/reference  (or set W4A16_REFERENCE)")
 sys.path.insert(0, os.path.join(REF, "src"))
 import w4a16 as R  # noqa: E402  (the reference package)
 

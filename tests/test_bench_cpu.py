@@ -51,3 +51,18 @@ def test_reference_arm_line():
     assert line["config"]["workload"] == "g128 int4 GEMV 262144x2048, batch 1"
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    # the full matrix every step (no extrapolation), and the reference's torch expression beside it
+    assert "full 262144x2048" in line["cpu_baseline"]["sample"] and "median" in line["cpu_baseline"]["sample"]
+    assert "same_inputs_as_gpu_arm" in line["config"]
+    assert line["reference_torch"]["value"] > 0 and "repeat_interleave" in line["reference_torch"]["expr"]
+
+
+def test_llama8b_shapes_shard_evenly_over_1_to_8_gpus():
+    from w4a16.tp import shard_bounds
+
+    for _, rows, cols in bench.LLAMA8B_SHAPES:
+        assert cols % 256 == 0                        # the TMA path of the kernel
+        for world in (1, 2, 4, 8):
+            spans = [shard_bounds(rows, world, r) for r in range(world)]
+            assert len({hi - lo for lo, hi in spans}) == 1, (rows, world)  # equal shards
+            assert (spans[0][1] - spans[0][0]) % 16 == 0

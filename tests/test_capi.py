@@ -173,3 +173,10 @@ def test_tensor_parallel_host_validation(lib):
     assert call(regions=((1 << 20), 0)) == -1
     assert call(cols=200) == -2
     assert call(flags=2) == -4
+    # regions the process neither allocated nor opened: their capacity is unknown
+    assert call() == -2
+    assert b"w4a16_tp_region_alloc" in lib.w4a16_last_error_string()
+    assert lib.w4a16_tp_set_peer_wait_ns(999) == -2
+    assert lib.w4a16_tp_set_peer_wait_ns(61 * 10**9) == -2
+    assert lib.w4a16_tp_set_peer_wait_ns(50 * 10**6) == 0
+    assert lib.w4a16_tp_set_peer_wait_ns(0) == 0

@@ -156,3 +156,61 @@ def test_fused_allgather_host_logic(world, rows):
         assert launches == [(hi - lo, 256, lo, rank, world, want)]
         assert out_ptr == want[rank] + 256                      # output after the header
         assert sorted(closed) == sorted([(w, 0) for k, w in enumerate(want) if k != rank] + [(want[rank], 1)])
+
+
+# Llama-3-8B-shaped projections (q, k = v, gate = up, down, head), group-128
+LLAMA8B_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+
+
+def _llama8b_worker(rank, world, port, q):
+    from oracle import c_oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        threads = max(1, (os.cpu_count() or 2) // world)
+        out = []
+        for rows, cols in LLAMA8B_SHAPES:
+            rng = np.random.default_rng(rows + cols)   # the same matrix on every rank
+            packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+            scale = (rng.random((rows, cols // 128), dtype=np.float32) * 2e-3 + 2e-3)
+            for batch in (1, 4, 16):
+                if rows == 128256 and batch == 4:
+                    continue  # the head at batch 1 and 16 is enough here
+                x = rng.standard_normal((batch, cols)).astype(np.float16)
+
+                def local_gemv(p_, s_, x_, res):
+                    res.copy_(torch.from_numpy(c_oracle.gemv(p_.numpy(), s_.numpy(), x_.numpy(), group=128,
+                                                             threads=threads)))
+
+                tp = RowShardedW4A16(shard_rows(torch.from_numpy(packed), world, rank),
+                                     shard_rows(torch.from_numpy(scale), world, rank), rows, group=128,
+                                     gemv_fn=local_gemv)
+                y = tp(torch.from_numpy(x if batch > 1 else x[0]))
+                ref = c_oracle.gemv(packed, scale, x, group=128, threads=threads)
+                ref = ref if batch > 1 else ref[0]
+                out.append((rows, cols, batch, tuple(y.shape), float(np.abs(y.numpy() - ref).max())))
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_llama8b_shapes_row_sharded_gather(world):
+    """The Llama-3-8B-shaped layers at batch 1, 4 and 16 sharded over 2 and 3 CPU ranks:
+    the gathered output equals the product over the whole matrix (same summation per row)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_llama8b_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, cases in results:
+        assert len(cases) == 14
+        for rows, cols, batch, shape, err in cases:
+            assert shape == ((rows,) if batch == 1 else (batch, rows))
+            assert err == 0.0, f"rank {rank} {rows}x{cols} batch {batch}: max err {err}"

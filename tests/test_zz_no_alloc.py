@@ -5,8 +5,9 @@ that passes only input and output buffers, so they cannot give the library a
 workspace.  This entry point takes its split-K scratch from an array inside the
 library instead.  The test calls it through the C ABI twice in a row (the second
 call sees the array as the first left it) and compares each result with the
-existing entry point w4a16_gemv run with its own workspace.  This file is collected
-last so that a run stopping at the first failure has already run the other tests.
+existing entry point w4a16_gemv run with its own workspace, and with the oracle.
+This file is collected last so that a run stopping at the first failure has already
+run the other tests.
 """
 import ctypes
 
@@ -15,6 +16,7 @@ import pytest
 import torch
 
 import w4a16 as K
+from oracle import c_oracle
 from w4a16 import _lib
 
 pytestmark = pytest.mark.gpu
@@ -49,10 +51,14 @@ def test_noalloc_matches_workspace_entry_two_calls(rows, cols, group, sdt):
     x = torch.randn(cols, device=DEV, generator=g).half()
     packed, scale = K.quantize_pack(w, group=group, scale_dtype=sdt)
     ref = K.gemv(packed, scale, x, group=group).cpu().numpy().astype(np.float64)
+    oracle = c_oracle.gemv(packed.cpu().numpy(), scale.float().cpu().numpy(), x.cpu().numpy(),
+                           group=group).astype(np.float64)
     for _ in range(2):
         y = _noalloc(packed, scale, x, group).cpu().numpy().astype(np.float64)
         err = np.abs(y - ref)
         assert (err <= ATOL + RTOL * np.abs(ref)).all(), f"max abs err {err.max():.3e}"
+        err = np.abs(y - oracle)
+        assert (err <= ATOL + RTOL * np.abs(oracle)).all(), f"max abs err vs oracle {err.max():.3e}"
 
 
 def test_noalloc_scratch_does_not_grow_with_the_matrix():

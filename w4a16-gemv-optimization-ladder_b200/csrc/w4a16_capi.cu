@@ -5,6 +5,10 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
+
 #include "w4a16_b200.h"
 #include "w4a16_internal.h"
 
@@ -15,6 +19,36 @@ using w4a16::set_error;
 constexpr int kVersion = 1 * 10000 + 0 * 100 + 0;
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Tensor-parallel regions known to this process (created by w4a16_tp_region_alloc or
+// mapped by w4a16_tp_region_open), with the byte capacity of each one's gathered output.
+// The fused all-gather stores every rank's rows into every region, so a call whose rows
+// do not fit one of them is rejected before launch.  The capacity also sits in the
+// region's header (kTpCapacityOffset), where the opening process reads it.
+std::mutex g_region_mu;
+std::unordered_map<uintptr_t, size_t> g_region_capacity;
+
+void register_region(void* region, size_t out_bytes) {
+  std::lock_guard<std::mutex> lock(g_region_mu);
+  g_region_capacity[reinterpret_cast<uintptr_t>(region)] = out_bytes;
+}
+
+void forget_region(void* region) {
+  std::lock_guard<std::mutex> lock(g_region_mu);
+  g_region_capacity.erase(reinterpret_cast<uintptr_t>(region));
+}
+
+bool region_capacity(const void* region, size_t* out_bytes) {
+  std::lock_guard<std::mutex> lock(g_region_mu);
+  const auto it = g_region_capacity.find(reinterpret_cast<uintptr_t>(region));
+  if (it == g_region_capacity.end()) return false;
+  *out_bytes = it->second;
+  return true;
+}
+
+// Limit of the fused all-gather's waits on other GPUs (0 = the 2 s default).
+std::atomic<unsigned long long> g_peer_wait_ns{0};
+constexpr unsigned long long kDefaultPeerWaitNs = 2000000000ull;
 
 // Shape / pointer checks shared by every GEMV-style entry point.
 int check_gemv(const void* packed, int packing, const void* scale, int scale_dtype, int group,
@@ -285,6 +319,11 @@ int w4a16_tp_region_alloc(size_t out_bytes, void** region, void* ipc_handle) {
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, w4a16::kTpHeaderBytes + out_bytes);
   if (e == cudaSuccess) e = cudaMemset(p, 0, w4a16::kTpHeaderBytes + out_bytes);
+  if (e == cudaSuccess) {  // the output capacity, for the processes that open the region
+    const unsigned long long cap = out_bytes;
+    e = cudaMemcpy(static_cast<uint8_t*>(p) + w4a16::kTpCapacityOffset, &cap, sizeof(cap),
+                   cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
@@ -294,6 +333,7 @@ int w4a16_tp_region_alloc(size_t out_bytes, void** region, void* ipc_handle) {
     return W4A16_ERR_CUDA;
   }
   memcpy(ipc_handle, &h, sizeof(h));
+  register_region(p, out_bytes);
   *region = p;
   return W4A16_OK;
 }
@@ -306,17 +346,27 @@ int w4a16_tp_region_open(const void* ipc_handle, void** region) {
   cudaIpcMemHandle_t h;
   memcpy(&h, ipc_handle, sizeof(h));
   void* p = nullptr;
-  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
   if (e != cudaSuccess) {
     set_error("cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
     return W4A16_ERR_CUDA;
   }
+  unsigned long long cap = 0;  // written into the header by the owner's w4a16_tp_region_alloc
+  e = cudaMemcpy(&cap, static_cast<uint8_t*>(p) + w4a16::kTpCapacityOffset, sizeof(cap),
+                 cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    cudaIpcCloseMemHandle(p);
+    set_error("reading the capacity of an opened region: %s", cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  register_region(p, (size_t)cap);
   *region = p;
   return W4A16_OK;
 }
 
 int w4a16_tp_region_close(void* region, int owned) {
   if (!region) return W4A16_OK;
+  forget_region(region);
   const cudaError_t e = owned ? cudaFree(region) : cudaIpcCloseMemHandle(region);
   if (e != cudaSuccess) {
     set_error("closing a tensor-parallel region: %s", cudaGetErrorString(e));
@@ -351,6 +401,23 @@ int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dty
   int rc = check_gemv(packed, W4A16_PACK_INTERLEAVED, scale, scale_dtype, group, x, 1, rows, cols,
                       mine, out_dtype);
   if (rc != W4A16_OK) return rc;
+  {  // rows [row0, row0 + rows) are stored into every region: each must hold them
+    const size_t esize = out_dtype == W4A16_DTYPE_F32 ? 4 : 2;
+    const unsigned long long end = ((unsigned long long)row0 + (unsigned long long)rows) * esize;
+    for (int k = 0; k < nranks; ++k) {
+      size_t cap = 0;
+      if (!region_capacity(regions[k], &cap)) {
+        set_error("region %d was not created by w4a16_tp_region_alloc or mapped by "
+                  "w4a16_tp_region_open in this process", k);
+        return W4A16_ERR_SHAPE;
+      }
+      if (end > cap) {
+        set_error("rows [%lld, %lld) of %zu-byte outputs do not fit region %d (%zu bytes)", row0,
+                  row0 + rows, esize, k, cap);
+        return W4A16_ERR_SHAPE;
+      }
+    }
+  }
   if (cols % 256 != 0 || !aligned(packed, 16)) {
     set_error("fused all-gather needs cols %% 256 == 0 (got %d) and 16-byte aligned weights", cols);
     return cols % 256 != 0 ? W4A16_ERR_SHAPE : W4A16_ERR_ALIGN;
@@ -376,9 +443,20 @@ int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dty
     p.tp_flags[k] = static_cast<unsigned*>(regions[k]);
     p.tp_out[k] = static_cast<uint8_t*>(regions[k]) + w4a16::kTpHeaderBytes;
   }
+  const unsigned long long wait = g_peer_wait_ns.load(std::memory_order_relaxed);
+  p.tp_wait_ns = wait ? wait : kDefaultPeerWaitNs;
   p.pdl = (flags & W4A16_LAUNCH_PDL) != 0;
   p.stream = reinterpret_cast<cudaStream_t>(stream);
   return w4a16::launch_gemv(p);
+}
+
+int w4a16_tp_set_peer_wait_ns(unsigned long long ns) {
+  if (ns != 0 && (ns < 1000ull || ns > 60000000000ull)) {
+    set_error("peer wait limit %llu ns outside [1 us, 60 s] (0 restores the 2 s default)", ns);
+    return W4A16_ERR_SHAPE;
+  }
+  g_peer_wait_ns.store(ns, std::memory_order_relaxed);
+  return W4A16_OK;
 }
 
 size_t w4a16_gemv_workspace_bytes(int batch, int rows, int cols) {

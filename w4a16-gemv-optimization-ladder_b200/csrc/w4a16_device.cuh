@@ -95,6 +95,18 @@ __device__ __forceinline__ void decode_word_fold(uint32_t w, uint32_t (&o)[4]) {
   o[3] = lop3_and_or(w8, kHiMask, kExp64x2);
 }
 
+// Every nibble left biased: o[0] and o[2] hold 1024 + n = q + 1032, o[1] and o[3] hold
+// 64 + n = q + 72, all exact.  Five instructions: one shift, four lop3.  The caller
+// removes 1032 * (sum of x over columns 0,1,4,5 of every 8) + 72 * (sum over 2,3,6,7)
+// per group (interleaved packing).
+__device__ __forceinline__ void decode_word_fold_all(uint32_t w, uint32_t (&o)[4]) {
+  const uint32_t w8 = w >> 8;
+  o[0] = lop3_and_or(w, kLoMask, kExp16x2);
+  o[1] = lop3_and_or(w, kHiMask, kExp64x2);
+  o[2] = lop3_and_or(w8, kLoMask, kExp16x2);
+  o[3] = lop3_and_or(w8, kHiMask, kExp64x2);
+}
+
 // Reorder an 8-column activation chunk (four f16x2: (x0,x1) (x2,x3) (x4,x5) (x6,x7))
 // into the column pairs that decode_word produces for the simple packing:
 // (x1,x5) (x0,x4) (x3,x7) (x2,x6).

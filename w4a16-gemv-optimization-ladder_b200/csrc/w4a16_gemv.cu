@@ -50,6 +50,12 @@
 #ifndef W4A16_FOLD  // batch-1 decode with half the nibbles left biased (decode_word_fold)
 #define W4A16_FOLD 1
 #endif
+#ifndef W4A16_FOLD_LO  // group-128 batch-1 decode with every nibble left biased (decode_word_fold_all)
+#define W4A16_FOLD_LO 0
+#endif
+#ifndef W4A16_ROW_NORESET  // per-row batch-1: one accumulation per tile, bias removed once per window
+#define W4A16_ROW_NORESET 1
+#endif
 #ifndef W4A16_TMA_WARPS
 #define W4A16_TMA_WARPS 12
 #endif
@@ -82,7 +88,6 @@ constexpr int kTpStart = 0;                 // u32 [kMaxRanks]
 constexpr int kTpDone = kMaxRanks;          // u32 [kMaxRanks]
 constexpr int kTpEpoch = 2 * kMaxRanks;     // u32
 constexpr int kTpCtaDone = 2 * kMaxRanks + 1;
-constexpr uint64_t kPeerWaitLimitNs = 2000000000ull;  // 2 s
 
 constexpr uint64_t kStageWaitLimitNs = 2000000000ull;  // 2 s; a stage normally lands in us
 constexpr uint64_t kDrainWaitLimitNs = 100000000ull;   // 0.1 s per outstanding stage
@@ -121,6 +126,7 @@ struct TmaParams {
   // gathered output tp_out[k]; tp_flags[k] is rank k's header
   int tp_n, tp_rank;
   long long tp_row0;
+  unsigned long long tp_wait_ns;  // limit of each wait on another rank's flags
   void* tp_out[kMaxRanks];
   unsigned* tp_flags[kMaxRanks];
 };
@@ -239,10 +245,17 @@ __device__ __forceinline__ LaneOffsets lane_offsets(int g, int t) {
 }
 
 // FOLD (one activation vector, interleaved packing): weights decoded with
-// decode_word_fold; every 128-column group starts its accumulator at corr[group] =
-// -72 * (sum of x over the group's biased columns), which cancels the bias exactly up
-// to fp32 rounding, and is then added (scaled, for group-128) into tot.
-template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS, bool FOLD>
+// decode_word_fold (or, with FOLD_LO, decode_word_fold_all), leaving a known bias on
+// the codes; corr[group] = -(bias x sum of x over the group's biased columns) cancels it
+// exactly up to fp32 rounding.
+//   group-128: every group's accumulation starts from C = 0 and its sum enters tot as
+//              scale * (acc + corr[group]);
+//   per-row (ROWFOLD): one accumulation runs over the whole tile segment, and the
+//              window's correction (the sum of its groups' corr) is added once per
+//              window in the epilogue; the bias of one row stays a few thousand at
+//              most, where fp32 keeps ~1e-4 absolute.
+template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS, bool FOLD,
+          bool FOLDLO>
 __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, uint32_t xs,
                                                uint32_t corr, int nslab, int kcol0,
                                                const TmaParams& p, int g, int t,
@@ -253,13 +266,15 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
   const uint32_t xwin = xs + lo.x + (uint32_t)(kcol0 >> 7) * 256u;
   constexpr int NH = BatchCfg<NB>::kHalves;
   constexpr int kGroups = SLABS * 2;
+  constexpr bool ROWFOLD = FOLD && !GS && W4A16_ROW_NORESET;
   static_assert(!FOLD || (NB == 1 && PACK == W4A16_PACK_INTERLEAVED), "FOLD: one vector, interleaved");
+  static_assert(!FOLDLO || (FOLD && GS), "FOLDLO: group-128 folded decode only");
 #pragma unroll
   for (int sl = 0; sl < SLABS; ++sl) {
     if (FULL || sl < nslab) {
       const int kcol = kcol0 + sl * kSlabCols;
       float cinit[2] = {0.f, 0.f};
-      if (FOLD) {
+      if (FOLD && !ROWFOLD) {
 #pragma unroll
         for (int gh = 0; gh < 2; ++gh) cinit[gh] = lds_f32(corr + (uint32_t)((kcol >> 7) + gh) * 4u);
       }
@@ -292,7 +307,10 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
             const uint32_t word_a = j == 0 ? va.x : j == 1 ? va.y : j == 2 ? va.z : va.w;
             const uint32_t word_b = j == 0 ? vb.x : j == 1 ? vb.y : j == 2 ? vb.z : vb.w;
             uint32_t A[4], B[4];
-            if (FOLD) {
+            if (FOLDLO) {
+              decode_word_fold_all(word_a, A);
+              decode_word_fold_all(word_b, B);
+            } else if (FOLD) {
               decode_word_fold(word_a, A);
               decode_word_fold(word_b, B);
             } else {
@@ -301,10 +319,10 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
             }
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
-              if (FOLD && j == 0)
-                mma_16816_c(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y, cinit[gh]);
-              else if (GS && j == 0)
+              if (GS && j == 0)  // every group-128 sum starts from zero
                 mma_16816_zc(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
+              else if (FOLD && !ROWFOLD && j == 0)
+                mma_16816_c(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y, cinit[gh]);
               else
                 mma_16816(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
               mma_16816(acc[rt][gh][h], A[2], B[2], A[3], B[3], xv[h].z, xv[h].w);
@@ -327,15 +345,18 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
               s0 = __half2float(__ushort_as_half(lds_u16(sbase + (ra * kGroups + grp) * 2)));
               s1 = __half2float(__ushort_as_half(lds_u16(sbase + ((ra + 8) * kGroups + grp) * 2)));
             }
+            // FOLD: the group's bias correction joins its sum before the scale
+            const float cg = FOLD ? cinit[gh] : 0.f;
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
-              tot[rt][h][0] = fmaf(s0, acc[rt][gh][h][0], tot[rt][h][0]);
-              tot[rt][h][1] = fmaf(s0, acc[rt][gh][h][1], tot[rt][h][1]);
-              tot[rt][h][2] = fmaf(s1, acc[rt][gh][h][2], tot[rt][h][2]);
-              tot[rt][h][3] = fmaf(s1, acc[rt][gh][h][3], tot[rt][h][3]);
+              // one activation vector: the MMA's columns are copies, only 0 and 2 are used
+              tot[rt][h][0] = fmaf(s0, FOLD ? acc[rt][gh][h][0] + cg : acc[rt][gh][h][0], tot[rt][h][0]);
+              if (NB != 1) tot[rt][h][1] = fmaf(s0, acc[rt][gh][h][1], tot[rt][h][1]);
+              tot[rt][h][2] = fmaf(s1, FOLD ? acc[rt][gh][h][2] + cg : acc[rt][gh][h][2], tot[rt][h][2]);
+              if (NB != 1) tot[rt][h][3] = fmaf(s1, acc[rt][gh][h][3], tot[rt][h][3]);
             }
           }
-      } else if (FOLD) {  // per-row scale: the groups are summed unscaled
+      } else if (FOLD && !ROWFOLD) {  // per-row scale: the groups are summed unscaled
 #pragma unroll
         for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -377,13 +398,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // weight copies are in flight.
   constexpr bool XS = XM != kXGlobal;
   constexpr bool FOLD = W4A16_FOLD && NB == 1 && PACK == W4A16_PACK_INTERLEAVED;
+  constexpr bool FOLDLO = FOLD && GS && W4A16_FOLD_LO;
+  constexpr bool ROWFOLD = FOLD && !GS && W4A16_ROW_NORESET;
   using Plan = SmemPlan<WARPS, STAGES, L>;
   // after the rings: [staged x: 2K bytes if XS][128-byte scratch][FOLD corrections:
-  // K/128 floats, 128-byte padded][kSchedLocal partial sums]
+  // K/128 group floats, then (ROWFOLD) nwin window sums, 128-byte padded][kSchedLocal
+  // partial sums]
   const uint32_t xs = base + (uint32_t)Plan::kXOff;
   const uint32_t red_off = XS ? (uint32_t)p.K * 2u : 0u;
   const uint32_t corr = xs + red_off + 128u;
-  const uint32_t corr_bytes = FOLD ? (uint32_t)(((p.K >> 7) * 4 + 127) & ~127) : 0u;
+  const uint32_t corr_bytes =
+      FOLD ? (uint32_t)((((p.K >> 7) + (ROWFOLD ? p.nwin : 0)) * 4 + 127) & ~127) : 0u;
+  const uint32_t corrw = corr + (uint32_t)(p.K >> 7) * 4u;  // ROWFOLD window sums
 
   const bool local = p.sched == kSchedLocal;
   const int ks = p.kslabs;
@@ -498,17 +524,37 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   }
 
   // FOLD: corr[g] = -72 * (sum of the fp16 activation over columns 8i+2, 8i+3, 8i+6,
-  // 8i+7 of group g), summed by the 16 threads holding the group's 16 chunks (a
-  // thread's chunks are warp-uniformly in or out of range: K is a multiple of 256).
+  // 8i+7 of group g) (FOLDLO: minus 1032 * the sum over columns 8i, 8i+1, 8i+4, 8i+5 as
+  // well), summed by the 16 threads holding the group's 16 chunks (a thread's chunks are
+  // warp-uniformly in or out of range: K is a multiple of 256).
   const int nch = p.K >> 3;  // 8-element chunks; thread i takes chunks i, i + blockDim, ...
   float* corr_f = reinterpret_cast<float*>(smem_raw + (corr - smem_addr(smem_raw)));
   auto fold_correction = [&](int c, const uint4& v) {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
     float part = (a.x + a.y) + (b.x + b.y);
+    float part_lo = 0.f;
+    if (FOLDLO) {
+      const float2 c2 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      const float2 d2 = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+      part_lo = (c2.x + c2.y) + (d2.x + d2.y);
+    }
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if ((lane & 15) == 0 && c < nch) corr_f[c >> 4] = -72.f * part;
+    for (int o = 1; o < 16; o <<= 1) {
+      part += __shfl_xor_sync(0xffffffffu, part, o);
+      if (FOLDLO) part_lo += __shfl_xor_sync(0xffffffffu, part_lo, o);
+    }
+    if ((lane & 15) == 0 && c < nch) corr_f[c >> 4] = FOLDLO ? -72.f * part - 1032.f * part_lo : -72.f * part;
+  };
+  // ROWFOLD: corr_f[K/128 + w] = sum of the corrections of window w's groups
+  auto window_corrections = [&]() {
+    const int ng = p.K >> 7;
+    for (int w = threadIdx.x; w < p.nwin; w += blockDim.x) {
+      float sum = 0.f;
+      for (int gi = w * 2 * SLABS; gi < ng && gi < (w + 1) * 2 * SLABS; ++gi) sum += corr_f[gi];
+      corr_f[ng + w] = sum;
+    }
+    __syncthreads();
   };
   if (FOLD && !XS) {  // the vector stays in global memory: read it once for the sums
     for (int c0 = 0; c0 < nch; c0 += blockDim.x) {
@@ -517,6 +563,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       fold_correction(c, v);
     }
     __syncthreads();
+    if (ROWFOLD) window_corrections();
   }
 
   if (XS) {
@@ -605,6 +652,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
     __syncthreads();
+    if (ROWFOLD) window_corrections();
   }
 
   // Fused all-gather.  CTA 0 announces step tp_e to every rank (the previous kernel has
@@ -625,7 +673,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       const uint64_t t0 = globaltimer_ns();
       for (int k = 0; k < p.tp_n && ok; ++k)
         while ((int)(ld_acquire_sys(tp_my + kTpStart + k) - tp_e) < 0) {
-          if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+          if (globaltimer_ns() - t0 > p.tp_wait_ns) {
             record_device_error(kDevErrPeerTimeout);
             ok = 0;
             break;
@@ -666,7 +714,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         const uint64_t t0 = globaltimer_ns();
         for (int k = 0; k < p.tp_n; ++k)
           while ((int)(ld_acquire_sys(tp_my + kTpDone + k) - tp_e) < 0) {
-            if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+            if (globaltimer_ns() - t0 > p.tp_wait_ns) {
               record_device_error(kDevErrPeerTimeout);
               break;
             }
@@ -684,6 +732,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   float tot[RT][NH][4];
   float acc[RT][2][NH][4];
   uint32_t srow_bits[RT][2];  // per-row scales (raw bits), converted in the epilogue
+  float csum = 0.f;           // ROWFOLD: bias correction of the segment's windows
   int tile = first_tile, win = first_win, tile_w0 = first_win;
 
 #pragma unroll 1
@@ -696,6 +745,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     }
     if (win == 0 || consumed == 0) {  // a tile starts in this warp's range
       tile_w0 = win;
+      csum = 0.f;
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt) {
 #pragma unroll
@@ -729,12 +779,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const uint32_t sbase = sring + slot * L::kSStride;
     const int s0 = win * SLABS;
     const int nslab = min(SLABS, ks - s0);
+    if (ROWFOLD) csum += lds_f32(corrw + (uint32_t)win * 4u);
     if (nslab == SLABS)
-      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS, FOLD>(wbase, sbase, xs, corr, nslab, s0 * kSlabCols,
-                                                            p, g, t, lo, acc, tot);
+      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(wbase, sbase, xs, corr, nslab,
+                                                                      s0 * kSlabCols, p, g, t, lo, acc, tot);
     else
-      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS, FOLD>(wbase, sbase, xs, corr, nslab, s0 * kSlabCols,
-                                                             p, g, t, lo, acc, tot);
+      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(wbase, sbase, xs, corr, nslab,
+                                                                       s0 * kSlabCols, p, g, t, lo, acc, tot);
     __syncwarp();  // every lane has read the slot before it is refilled
     issue_one();
 
@@ -753,7 +804,15 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       srow[rt][0] = GS ? 1.f : scale_from_bits<ST>(srow_bits[rt][0]);
       srow[rt][1] = GS ? 1.f : scale_from_bits<ST>(srow_bits[rt][1]);
     }
-    if (!GS && FOLD) {  // the groups were summed into tot: apply the row scale
+    if (ROWFOLD) {  // one accumulation per segment, minus the windows' bias
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          tot[rt][h][0] = (acc[rt][0][h][0] + acc[rt][1][h][0] + csum) * srow[rt][0];
+          tot[rt][h][2] = (acc[rt][0][h][2] + acc[rt][1][h][2] + csum) * srow[rt][1];
+        }
+    } else if (!GS && FOLD) {  // the groups were summed into tot: apply the row scale
 #pragma unroll
       for (int rt = 0; rt < RT; ++rt)
 #pragma unroll
@@ -1044,7 +1103,8 @@ constexpr int tma_smem_bytes() {
 template <int PACK, int NB, int XM>
 int tail_smem_bytes(int K) {
   constexpr bool fold = W4A16_FOLD && NB == 1 && PACK == W4A16_PACK_INTERLEAVED;
-  const int corr = fold ? ((K / 128) * 4 + 127) / 128 * 128 : 0;
+  // group corrections, plus one sum per 1024-column window (read by the per-row kernels)
+  const int corr = fold ? ((K / 128 + (K + 1023) / 1024) * 4 + 127) / 128 * 128 : 0;
   return (XM != kXGlobal ? K * 2 : 0) + (NB == 1 ? 128 : 0) + corr;
 }
 
@@ -1149,6 +1209,7 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   prm.tp_n = p.tp_n;
   prm.tp_rank = p.tp_rank;
   prm.tp_row0 = p.tp_row0;
+  prm.tp_wait_ns = p.tp_wait_ns;
   for (int k = 0; k < kMaxRanks; ++k) {
     prm.tp_out[k] = p.tp_out[k];
     prm.tp_flags[k] = p.tp_flags[k];

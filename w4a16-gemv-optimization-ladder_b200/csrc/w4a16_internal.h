@@ -38,6 +38,7 @@ struct GemvProblem {
   long long tp_row0 = 0;            // this rank's first row in the gathered output
   void* tp_out[8] = {};             // every rank's gathered output
   unsigned* tp_flags[8] = {};       // every rank's region header
+  unsigned long long tp_wait_ns = 0;  // limit of each wait on another rank's flags
   bool staged = false;              // fused entry: x staged in shared memory, TMA kernel only
   bool pdl = false;                 // programmatic dependent launch (staged GEMV only)
   cudaStream_t stream = nullptr;
@@ -98,8 +99,11 @@ cudaError_t launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Fused all-gather: bytes of the flag header at the start of every rank's region.
+// Fused all-gather: bytes of the flag header at the start of every rank's region, and
+// the header offset of the region's output capacity in bytes (u64, written once by
+// w4a16_tp_region_alloc; the kernels use header bytes [0, 128) for their flags).
 constexpr size_t kTpHeaderBytes = 256;
+constexpr size_t kTpCapacityOffset = 128;
 
 // Reads (and clears) the device-side error word written by kernels whose bounded
 // waits ran out.  Synchronises `stream`.

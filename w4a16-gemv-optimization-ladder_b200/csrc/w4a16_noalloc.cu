@@ -20,7 +20,11 @@
 // Host code never uses the array's name as a device address (on the host it names a
 // stand-in object).  The first call on each device, with that device current, asks
 // the runtime for the array's device address with cudaGetSymbolAddress and caches
-// it; make that first call before any stream capture on the device.
+// it; make that first call before any stream capture on the device.  The cache is
+// keyed by the device and by its current CUDA context, so a caller that switches to
+// another context, or whose context was destroyed (cudaDeviceReset) and recreated,
+// gets the address looked up again in the new context.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -37,8 +41,26 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device (set up once per device).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// cuCtxGetCurrent from the driver the runtime already loaded (no link against libcuda).
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
+
+// Device address of the scratch array on the current device, looked up once per
+// (device, context) and cached.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -50,15 +72,25 @@ int scratch_address(void** out) {
     w4a16::set_error("device index %d out of range", dev);
     return W4A16_ERR_CUDA;
   }
+  CtxGetCurrentFn get_ctx = ctx_get_current();
+  if (!get_ctx) {
+    w4a16::set_error("cuCtxGetCurrent is unavailable");
+    return W4A16_ERR_CUDA;
+  }
+  CUcontext ctx = nullptr;  // null while no context is current on this thread
+  if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_addr[dev]) {
+  if (!ctx || !g_scratch_addr[dev] || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
+    // (makes the device's primary context current when none is)
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
       w4a16::set_error("cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
       return W4A16_ERR_CUDA;
     }
+    if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_addr[dev];
   return W4A16_OK;

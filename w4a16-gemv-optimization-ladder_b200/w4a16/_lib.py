@@ -52,6 +52,7 @@ SIGNATURES = {
     "w4a16_tp_region_close": ([_p, _i], _i),
     "w4a16_gemv_allgather": ([_p, _p, _i, _i, _p, _i, _i, _i, ctypes.c_longlong, _i, _i,
                               ctypes.POINTER(ctypes.c_void_p), _p, _sz, _u, _p], _i),
+    "w4a16_tp_set_peer_wait_ns": ([ctypes.c_ulonglong], _i),
     "w4a16_gemv_noalloc": ([_p, _p, _i, _i, _p, _i, _i, _p, _p], _i),
     "w4a16_dequant": ([_p, _i, _p, _i, _i, _i, _i, _p, _p], _i),
     "w4a16_quantize_pack": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p], _i),

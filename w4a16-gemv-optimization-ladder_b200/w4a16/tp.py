@@ -161,10 +161,12 @@ class FusedAllGatherW4A16:
     def _make_out(self, ptr, n, dtype):
         return torch.as_tensor(_DeviceArray(ptr, n, dtype), device=self.device)
 
-    def launch(self, packed, scale, x, stream=None, pdl=False):
+    def launch(self, packed, scale, x, stream=None, pdl=False, check=False):
         """One step with explicit weights (this rank's rows), for callers that alternate
         several weight copies of the same shape.  pdl: chain to the previous kernel on the
-        stream (programmatic dependent launch); the workspaces alternate per call."""
+        stream (programmatic dependent launch); the workspaces alternate per call.
+        check: wait for the step and raise if a wait on another rank ran out (see
+        device_error); without it the step stays asynchronous."""
         from . import _lib
         from . import kernels as K
 
@@ -178,14 +180,37 @@ class FusedAllGatherW4A16:
             self._regions, ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
             ws.numel() if ws is not None else 0, _lib.LAUNCH_PDL if pdl else 0, s)
         self._check(st, "w4a16_gemv_allgather")
+        if check:
+            code = self.device_error(stream=s)
+            if code:
+                raise RuntimeError(f"w4a16_gemv_allgather: device error {code} (a rank's flags did not "
+                                   "arrive in time; only this rank's rows of the output are current)")
         return self.out
 
-    def __call__(self, x, pdl=False):
+    def device_error(self, stream=None):
+        """Read and clear the device error word after the steps issued so far (synchronises
+        the stream): 0 = every step assembled the whole output; 2 = a wait on another rank
+        ran out, and that step wrote only this rank's rows.  After a non-zero code the
+        ranks' step numbers disagree: close this object and build a new one.  The split-K
+        workspaces are zero-filled again, as a warp that gave up may have left counters."""
+        from . import _lib
+        from . import kernels as K
+
+        s = stream if stream is not None else K._stream(self.device)
+        code = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            self._check(self.lib.w4a16_read_device_error(ctypes.byref(code), s), "w4a16_read_device_error")
+            if code.value and self.workspaces is not None:
+                for w in self.workspaces:
+                    w.zero_()
+        return code.value
+
+    def __call__(self, x, pdl=False, check=False):
         if not (isinstance(x, torch.Tensor) and x.dtype == torch.float16 and x.dim() == 1
                 and x.is_contiguous() and x.shape[0] == self.packed.shape[1] * 2 and x.device == self.device):
             raise RuntimeError("x must be a contiguous fp16 [cols] tensor on this rank's device")
         with torch.cuda.device(self.device):
-            return self.launch(self.packed, self.scale, x, pdl=pdl)
+            return self.launch(self.packed, self.scale, x, pdl=pdl, check=check)
 
     def close(self):
         """Unmap the peers' regions and free this rank's (after every rank is done)."""
