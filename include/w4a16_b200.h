@@ -212,6 +212,85 @@ int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dty
  * missing rank quickly (a failure-detection test, a watchdog) get the error code sooner. */
 int w4a16_tp_set_peer_wait_ns(unsigned long long ns);
 
+/* ---------------------------------------------------------------------------
+ * One-kernel decode step of a Llama-architecture model (no counterpart in the reference,
+ * whose end-to-end decode runs the Hugging Face model with its GEMV swapped into every
+ * Linear: benchmarks/end_to_end.py:24-42).  One persistent launch per token runs every
+ * layer's RMSNorm + QKV GEMV, rotary + KV-cache write + attention, output GEMV + residual,
+ * RMSNorm + gate|up GEMV, SwiGLU + down GEMV + residual, then the final norm and the head,
+ * with grid-wide barriers between the phases; all projections are int4 with group-128
+ * fp32 scales on the interleaved packing.
+ * ------------------------------------------------------------------------- */
+
+/* One projection: packed uint8 [rows][cols/2] and fp32 scales [rows][cols/128], both
+ * 16-byte aligned device memory. */
+typedef struct {
+  const uint8_t* packed;
+  const float* scale;
+} w4a16_g128_weight;
+
+/* A model.  The arrays are host arrays of `layers` entries (read by
+ * w4a16_decode_plan_create only); every pointer they hold, and every other pointer, is
+ * device memory that must stay valid while the plan is used.
+ *   qkv      rows (heads + 2 kv_heads) * head_dim (q | k | v), cols hidden
+ *   o        rows hidden, cols heads * head_dim
+ *   gate_up  rows 2 * intermediate, cols hidden: gate | up (gate_up_interleaved 0), or gate and
+ *            up interleaved in blocks of 8 rows (gate_up_interleaved 8: rows 16k..16k+7 are gate
+ *            rows 8k..8k+7, rows 16k+8..16k+15 the matching up rows), which lets the step apply
+ *            SwiGLU in the projection's epilogue instead of in the next phase
+ *   down     rows hidden, cols intermediate
+ *   lm_head  rows vocab, cols hidden
+ *   norm_*   fp32 [hidden] RMSNorm weights; embed fp16 [vocab][hidden];
+ *   rope_cos, rope_sin  fp32 [max_len][head_dim] rotate-half tables.
+ * Limits: head_dim 64; hidden, intermediate and heads * 64 multiples of 1024; hidden at most
+ * 4096, intermediate and heads * 64 at most 8192; heads a multiple of kv_heads, at most 8
+ * query heads per kv head (Llama-3.2-1B: 2048, 8192, 32 x 64, 4 per kv head). */
+typedef struct {
+  int layers, hidden, intermediate, heads, kv_heads, head_dim, vocab, max_len;
+  float eps;
+  const w4a16_g128_weight* qkv;
+  const w4a16_g128_weight* o;
+  const w4a16_g128_weight* gate_up;
+  const w4a16_g128_weight* down;
+  const float* const* norm_attn;
+  const float* const* norm_mlp;
+  w4a16_g128_weight lm_head;
+  const float* norm_final;
+  const void* embed;
+  const float* rope_cos;
+  const float* rope_sin;
+  int gate_up_interleaved;
+} w4a16_llama_desc;
+
+typedef struct w4a16_decode_plan_st* w4a16_decode_plan;
+
+/* Builds the step's tables (tensor maps of every projection) and allocates its scratch on
+ * the current device (cudaMalloc; it synchronises the device).  One plan per model and
+ * device; free it with w4a16_decode_plan_destroy. */
+int w4a16_decode_plan_create(const w4a16_llama_desc* desc, w4a16_decode_plan* plan);
+int w4a16_decode_plan_destroy(w4a16_decode_plan plan);
+
+/* One decode step for the token *token at position *pos (device int64 scalars, read by the
+ * kernel, so a CUDA graph can replay the step with new values): writes the rotated key and
+ * the value of every layer into the caches at pos (fp16 [layers][kv_heads][max_len][64]
+ * each) and the logits (fp32 [vocab]).  A pos outside [0, max_len) or a token outside
+ * [0, vocab) writes no cache row and gives NaN logits.  Steps of one plan share its scratch:
+ * order them on one stream.  Every wait in the kernel is bounded: a wait that runs out sets
+ * the device error word (w4a16_read_device_error: 1 weight copy, 3 grid barrier). */
+int w4a16_decode_step(w4a16_decode_plan plan, const int64_t* token, const int64_t* pos,
+                      void* k_cache, void* v_cache, float* logits, w4a16_stream_t stream);
+
+/* Timeline of the decode step, for finding where a step's time goes.  enable != 0 makes the
+ * following steps record %globaltimer (ns) per CTA: entry cta the start, grid + cta the end,
+ * 2 grid + cta the moment the first phase's input vector is in place, then for barrier
+ * b = 1..5*layers the arrival (3b*grid + cta), the departure ((3b+1)*grid + cta) and the
+ * moment the next phase's input is in place ((3b+2)*grid + cta; the attention phase stamps
+ * its start); *count receives the number of entries.  With host != NULL
+ * (capacity >= *count) the last step's record is copied out (synchronises the stream).
+ * enable == 0 stops recording and frees the buffer. */
+int w4a16_decode_plan_timeline(w4a16_decode_plan plan, int enable, unsigned long long* host,
+                               size_t capacity, size_t* count, w4a16_stream_t stream);
+
 /* Bytes of workspace that let w4a16_gemv balance its work across warps (stream-K)
  * for this batch size; independent of rows and cols (about 0.5 MiB per activation
  * row, at most 16 of them per pass). */
@@ -249,7 +328,7 @@ int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int grou
 
 /* Reads and clears the error word that kernels set when a bounded wait runs out
  * (0 = none; 1 = a weight copy did not land in time; 2 = another rank's flag did not
- * arrive in time).  Synchronises `stream`.  A non-zero code means some warps returned
+ * arrive in time; 3 = a grid barrier of w4a16_decode_step timed out).  Synchronises `stream`.  A non-zero code means some warps returned
  * early: their rows of the output are missing, and a split-K workspace they used may hold
  * non-zero counters, so zero-fill again every workspace used since the previous read
  * (w4a16_gemv_noalloc clears its own on every call). */

@@ -180,3 +180,33 @@ def test_tensor_parallel_host_validation(lib):
     assert lib.w4a16_tp_set_peer_wait_ns(61 * 10**9) == -2
     assert lib.w4a16_tp_set_peer_wait_ns(50 * 10**6) == 0
     assert lib.w4a16_tp_set_peer_wait_ns(0) == 0
+
+
+def test_decode_plan_host_validation(lib):
+    """The one-kernel decode step checks its model description on the host before any
+    CUDA call (no GPU needed for these answers)."""
+    from w4a16.decode import _G128Weight, _LlamaDesc
+
+    plan = ctypes.c_void_p()
+    assert lib.w4a16_decode_plan_create(None, ctypes.byref(plan)) == -1
+    assert lib.w4a16_decode_plan_create(None, None) == -1
+    w = (_G128Weight * 1)(_G128Weight(1 << 12, 1 << 12))
+    n = (ctypes.c_void_p * 1)(1 << 12)
+
+    def desc(**kw):
+        f = dict(layers=1, hidden=2048, intermediate=8192, heads=32, kv_heads=8, head_dim=64, vocab=1000,
+                 max_len=64, eps=1e-5)
+        f.update(kw)
+        return _LlamaDesc(f["layers"], f["hidden"], f["intermediate"], f["heads"], f["kv_heads"], f["head_dim"],
+                          f["vocab"], f["max_len"], f["eps"], w, w, w, w, n, n, _G128Weight(1 << 12, 1 << 12),
+                          1 << 12, 1 << 12, 1 << 12, 1 << 12)
+
+    for bad in (dict(head_dim=128), dict(hidden=2000), dict(heads=30), dict(heads=64, kv_heads=4),
+                dict(layers=0), dict(intermediate=32768), dict(max_len=0), dict(hidden=8192),
+                dict(intermediate=2560), dict(intermediate=9216), dict(heads=72, kv_heads=9)):
+        assert lib.w4a16_decode_plan_create(ctypes.byref(desc(**bad)), ctypes.byref(plan)) == -2, bad
+    assert b"unsupported decode-step shape" in lib.w4a16_last_error_string()
+    p = ctypes.c_void_p
+    assert lib.w4a16_decode_step(None, p(8), p(8), p(16), p(16), p(4), None) == -1
+    assert lib.w4a16_decode_step(p(1 << 12), p(8), p(12), p(16), p(16), p(4), None) == -3
+    assert lib.w4a16_decode_plan_destroy(None) == 0

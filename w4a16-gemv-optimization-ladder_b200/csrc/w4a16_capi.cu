@@ -498,7 +498,54 @@ int w4a16_read_device_error(int* code, w4a16_stream_t stream) {
     set_error("NULL code pointer");
     return W4A16_ERR_NULL;
   }
-  return w4a16::read_device_error(code, reinterpret_cast<cudaStream_t>(stream));
+  int a = 0, b = 0;
+  int rc = w4a16::read_device_error(&a, reinterpret_cast<cudaStream_t>(stream));
+  if (rc == W4A16_OK) rc = w4a16::read_decode_step_error(&b, reinterpret_cast<cudaStream_t>(stream));
+  if (rc != W4A16_OK) return rc;
+  *code = a ? a : b;
+  return W4A16_OK;
+}
+
+int w4a16_decode_plan_create(const w4a16_llama_desc* desc, w4a16_decode_plan* plan) {
+  if (!plan) {
+    set_error("null plan pointer");
+    return W4A16_ERR_NULL;
+  }
+  w4a16::DecodePlan* p = nullptr;
+  const int rc = w4a16::decode_plan_create(desc, &p);
+  *plan = reinterpret_cast<w4a16_decode_plan>(p);
+  return rc;
+}
+
+int w4a16_decode_plan_destroy(w4a16_decode_plan plan) {
+  return w4a16::decode_plan_destroy(reinterpret_cast<w4a16::DecodePlan*>(plan));
+}
+
+int w4a16_decode_plan_timeline(w4a16_decode_plan plan, int enable, unsigned long long* host,
+                               size_t capacity, size_t* count, w4a16_stream_t stream) {
+  if (!plan) {
+    set_error("null plan");
+    return W4A16_ERR_NULL;
+  }
+  return w4a16::decode_plan_timeline(reinterpret_cast<w4a16::DecodePlan*>(plan), enable, host, capacity,
+                                     count, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int w4a16_decode_step(w4a16_decode_plan plan, const int64_t* token, const int64_t* pos,
+                      void* k_cache, void* v_cache, float* logits, w4a16_stream_t stream) {
+  if (!plan || !token || !pos || !k_cache || !v_cache || !logits) {
+    set_error("null pointer argument");
+    return W4A16_ERR_NULL;
+  }
+  if (!aligned(token, 8) || !aligned(pos, 8) || !aligned(k_cache, 16) || !aligned(v_cache, 16) ||
+      !aligned(logits, 4)) {
+    set_error("token/pos need 8-byte, caches 16-byte, logits 4-byte alignment");
+    return W4A16_ERR_ALIGN;
+  }
+  return w4a16::decode_step_launch(reinterpret_cast<w4a16::DecodePlan*>(plan),
+                                   reinterpret_cast<const long long*>(token),
+                                   reinterpret_cast<const long long*>(pos), k_cache, v_cache, logits,
+                                   reinterpret_cast<cudaStream_t>(stream));
 }
 
 const char* w4a16_status_string(int status) {

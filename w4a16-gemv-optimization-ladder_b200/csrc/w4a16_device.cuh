@@ -323,6 +323,21 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Contiguous bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16),
+// completion signalled on `bar` (complete_tx).  The source is this GPU's own memory.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses to shared memory before later
+// async-proxy (TMA / bulk copy) writes to it.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
 template <>

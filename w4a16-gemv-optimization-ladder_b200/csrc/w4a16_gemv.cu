@@ -42,19 +42,11 @@
 #include <type_traits>
 
 #include "w4a16_device.cuh"
+#include "w4a16_gemv_core.cuh"
 #include "w4a16_internal.h"
 
 #ifndef W4A16_L2_PROMOTION  // L2 fill granularity of the weight copies (CU_TENSOR_MAP_L2_PROMOTION_*)
 #define W4A16_L2_PROMOTION 2  // 128 bytes (64, 128 and 256 measured within 0.2%)
-#endif
-#ifndef W4A16_FOLD  // batch-1 decode with half the nibbles left biased (decode_word_fold)
-#define W4A16_FOLD 1
-#endif
-#ifndef W4A16_FOLD_LO  // group-128 batch-1 decode with every nibble left biased (decode_word_fold_all)
-#define W4A16_FOLD_LO 0
-#endif
-#ifndef W4A16_ROW_NORESET  // per-row batch-1: one accumulation per tile, bias removed once per window
-#define W4A16_ROW_NORESET 1
 #endif
 #ifndef W4A16_TMA_WARPS
 #define W4A16_TMA_WARPS 12
@@ -94,8 +86,6 @@ constexpr uint64_t kDrainWaitLimitNs = 100000000ull;   // 0.1 s per outstanding 
 
 __device__ __forceinline__ void record_device_error(int code) { atomicCAS(&g_device_error, 0, code); }
 
-constexpr int kMmaRows = 16;      // rows of one m16n8k16 A fragment
-constexpr int kSlabCols = 256;    // columns per 128-byte slab of a packed row
 constexpr int kMaxBatchPerPass = 16;
 // Workspace layout: [counters: kMaxWarps x u32][fp32 partials: kMaxWarps x 2 slots x
 // batch x tile rows].  Counter w (< kMaxWarps - 2) belongs to the stream-K tile whose
@@ -162,213 +152,6 @@ struct LocalPlan {
   static constexpr int kUnits = WARPS * STAGES;
   static constexpr int kBytes = kUnits * ROWS * 4;
 };
-
-// Shared-memory stage of one warp: a window of SLABS 256-column slabs of RT*16 rows,
-// one 3-D TMA box laid out [row][slab][128 B] with the 128-byte swizzle (1024-byte
-// aligned), so every row of the box is one 512-byte run of global memory; and, for
-// group-128, the window's scale tile [row][2*SLABS].
-template <int SLABS, int RT, int GS, typename ST>
-struct StageLayout {
-  static_assert(SLABS == 4, "the swizzled [row][slab] layout is bank-conflict free for 4 slabs");
-  static constexpr int kRows = kMmaRows * RT;
-  static constexpr int kWBytes = kRows * SLABS * 128;
-  static constexpr int kWStride = (kWBytes + 1023) / 1024 * 1024;
-  static constexpr int kGroups = SLABS * 2;  // 128-column groups per window
-  static constexpr int kSBytes = GS ? kRows * kGroups * (int)sizeof(ST) : 0;
-  static constexpr int kSStride = (kSBytes + 127) / 128 * 128;
-  static constexpr bool kScaleBoxOk = !GS || (kGroups * sizeof(ST)) % 16 == 0;
-};
-
-// Shared-memory plan of one CTA (offsets from the 1024-byte aligned base):
-//   [W rings: WARPS x STAGES x kWStride][scale rings: WARPS x STAGES x kSStride]
-//   [mbarriers: WARPS x STAGES x 8][staged activation at a 128-byte boundary]
-template <int WARPS, int STAGES, typename L>
-struct SmemPlan {
-  static constexpr int kScaleOff = WARPS * STAGES * L::kWStride;
-  static constexpr int kBarOff = kScaleOff + WARPS * STAGES * L::kSStride;
-  static constexpr int kXOff = (kBarOff + WARPS * STAGES * 8 + 127) / 128 * 128;
-  // dynamic bytes requested: the plan plus slack for aligning the base to 1024
-  static constexpr int kBytes = kXOff + 1024;
-  static_assert(kScaleOff % 1024 == 0 && kBarOff % 16 == 0 && kXOff % 128 == 0, "smem alignment");
-};
-
-// Byte offset of logical 16-byte chunk c of (row r, slab sl) inside a stage.  The
-// 128-byte swizzle puts chunk c of 128-byte smem line L at c ^ (L & 7), L = 4r + sl:
-// rows g and g+8 of one MMA get the same XOR, and the two rows a quarter-warp reads
-// (g even and odd) get XORs that differ in bit 2, so its 8 lanes hit 8 bank groups.
-template <int SLABS>
-__device__ __forceinline__ uint32_t w_offset(int r, int sl, int c) {
-  const int line = r * SLABS + sl;
-  return (uint32_t)(line * 128 + ((c ^ (line & 7)) << 4));
-}
-
-template <int NB>
-struct BatchCfg {
-  static constexpr int kHalves = NB > 8 ? 2 : 1;  // n8 MMAs per A fragment
-};
-
-// Activation fragment for column block h: row n = h*8 + g of X (all rows = X[0]
-// when NB == 1, so every B column holds the single vector).
-template <int NB>
-__device__ __forceinline__ uint4 load_x(const __half* x, int K, int M, int g, int h, int col) {
-  if (NB == 1) return ldg128(x + col);
-  const int n = h * 8 + g;
-  if (n < M) return ldg128(x + (size_t)n * K + col);
-  return make_uint4(0u, 0u, 0u, 0u);
-}
-
-// One window of one warp: nslab (== SLABS when FULL) slabs of RT*16 rows.
-// Shared-memory copy of a single activation vector, ordered so that the B fragment
-// of (128-column group G, chunk j, thread t) is 16 bytes at ((G*4 + j)*4 + t)*16: the
-// four threads of a group read 64 contiguous bytes, one conflict-free wavefront.
-__device__ __forceinline__ uint32_t xs_offset(int col) {
-  const int grp = col >> 7, off = col & 127;
-  return (uint32_t)(((grp * 4 + ((off & 31) >> 3)) * 4 + (off >> 5)) * 16);
-}
-
-// Lane part of the weight-fragment offsets: for chunk c = gh*4 + t of slab sl in row
-// r = g (row g + 8 adds 8 lines = 4096 bytes, rt adds 16 rows), the swizzled offset
-// w_offset<4>(g, sl, c) depends only on the lane and (gh, sl): computed once.
-struct LaneOffsets {
-  uint32_t w[2][4];  // [gh][sl]
-  uint32_t x;        // t * 16 (fragment order of the staged activation)
-};
-
-__device__ __forceinline__ LaneOffsets lane_offsets(int g, int t) {
-  LaneOffsets o;
-#pragma unroll
-  for (int gh = 0; gh < 2; ++gh)
-#pragma unroll
-    for (int sl = 0; sl < 4; ++sl) o.w[gh][sl] = w_offset<4>(g, sl, gh * 4 + t);
-  o.x = (uint32_t)t * 16u;
-  return o;
-}
-
-// FOLD (one activation vector, interleaved packing): weights decoded with
-// decode_word_fold (or, with FOLD_LO, decode_word_fold_all), leaving a known bias on
-// the codes; corr[group] = -(bias x sum of x over the group's biased columns) cancels it
-// exactly up to fp32 rounding.
-//   group-128: every group's accumulation starts from C = 0 and its sum enters tot as
-//              scale * (acc + corr[group]);
-//   per-row (ROWFOLD): one accumulation runs over the whole tile segment, and the
-//              window's correction (the sum of its groups' corr) is added once per
-//              window in the epilogue; the bias of one row stays a few thousand at
-//              most, where fp32 keeps ~1e-4 absolute.
-template <bool FULL, bool XS, int PACK, int GS, typename ST, int NB, int RT, int SLABS, bool FOLD,
-          bool FOLDLO>
-__device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, uint32_t xs,
-                                               uint32_t corr, int nslab, int kcol0,
-                                               const TmaParams& p, int g, int t,
-                                               const LaneOffsets& lo,
-                                               float (&acc)[RT][2][BatchCfg<NB>::kHalves][4],
-                                               float (&tot)[RT][BatchCfg<NB>::kHalves][4]) {
-  // activation fragments of this window: 16 bytes at xwin + ((sl*2 + gh)*4 + j)*64
-  const uint32_t xwin = xs + lo.x + (uint32_t)(kcol0 >> 7) * 256u;
-  constexpr int NH = BatchCfg<NB>::kHalves;
-  constexpr int kGroups = SLABS * 2;
-  constexpr bool ROWFOLD = FOLD && !GS && W4A16_ROW_NORESET;
-  static_assert(!FOLD || (NB == 1 && PACK == W4A16_PACK_INTERLEAVED), "FOLD: one vector, interleaved");
-  static_assert(!FOLDLO || (FOLD && GS), "FOLDLO: group-128 folded decode only");
-#pragma unroll
-  for (int sl = 0; sl < SLABS; ++sl) {
-    if (FULL || sl < nslab) {
-      const int kcol = kcol0 + sl * kSlabCols;
-      float cinit[2] = {0.f, 0.f};
-      if (FOLD && !ROWFOLD) {
-#pragma unroll
-        for (int gh = 0; gh < 2; ++gh) cinit[gh] = lds_f32(corr + (uint32_t)((kcol >> 7) + gh) * 4u);
-      }
-      uint4 wa[RT][2], wb[RT][2];
-#pragma unroll
-      for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-        for (int gh = 0; gh < 2; ++gh) {
-          const int c = gh * 4 + t;
-          (void)c;
-          wa[rt][gh] = lds128(wbase + lo.w[gh][sl] + rt * 16 * SLABS * 128);
-          wb[rt][gh] = lds128(wbase + lo.w[gh][sl] + rt * 16 * SLABS * 128 + 8 * SLABS * 128);
-        }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-#pragma unroll
-        for (int gh = 0; gh < 2; ++gh) {
-          const int col = kcol + gh * 128 + 32 * t + 8 * j;
-          uint4 xv[NH];
-#pragma unroll
-          for (int h = 0; h < NH; ++h) {
-            xv[h] = XS ? lds128(xwin + ((sl * 2 + gh) * 4 + j) * 64)
-                       : load_x<NB>(p.x, p.K, p.M, g, h, col);
-            if (PACK == W4A16_PACK_SIMPLE) xv[h] = simple_order(xv[h]);
-          }
-#pragma unroll
-          for (int rt = 0; rt < RT; ++rt) {
-            const uint4& va = wa[rt][gh];
-            const uint4& vb = wb[rt][gh];
-            const uint32_t word_a = j == 0 ? va.x : j == 1 ? va.y : j == 2 ? va.z : va.w;
-            const uint32_t word_b = j == 0 ? vb.x : j == 1 ? vb.y : j == 2 ? vb.z : vb.w;
-            uint32_t A[4], B[4];
-            if (FOLDLO) {
-              decode_word_fold_all(word_a, A);
-              decode_word_fold_all(word_b, B);
-            } else if (FOLD) {
-              decode_word_fold(word_a, A);
-              decode_word_fold(word_b, B);
-            } else {
-              decode_word(word_a, A);
-              decode_word(word_b, B);
-            }
-#pragma unroll
-            for (int h = 0; h < NH; ++h) {
-              if (GS && j == 0)  // every group-128 sum starts from zero
-                mma_16816_zc(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
-              else if (FOLD && !ROWFOLD && j == 0)
-                mma_16816_c(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y, cinit[gh]);
-              else
-                mma_16816(acc[rt][gh][h], A[0], B[0], A[1], B[1], xv[h].x, xv[h].y);
-              mma_16816(acc[rt][gh][h], A[2], B[2], A[3], B[3], xv[h].z, xv[h].w);
-            }
-          }
-        }
-      }
-      if (GS) {
-#pragma unroll
-        for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-          for (int gh = 0; gh < 2; ++gh) {
-            const int grp = sl * 2 + gh;
-            const int ra = rt * 16 + g;
-            float s0, s1;
-            if (sizeof(ST) == 4) {
-              s0 = lds_f32(sbase + (ra * kGroups + grp) * 4);
-              s1 = lds_f32(sbase + ((ra + 8) * kGroups + grp) * 4);
-            } else {
-              s0 = __half2float(__ushort_as_half(lds_u16(sbase + (ra * kGroups + grp) * 2)));
-              s1 = __half2float(__ushort_as_half(lds_u16(sbase + ((ra + 8) * kGroups + grp) * 2)));
-            }
-            // FOLD: the group's bias correction joins its sum before the scale
-            const float cg = FOLD ? cinit[gh] : 0.f;
-#pragma unroll
-            for (int h = 0; h < NH; ++h) {
-              // one activation vector: the MMA's columns are copies, only 0 and 2 are used
-              tot[rt][h][0] = fmaf(s0, FOLD ? acc[rt][gh][h][0] + cg : acc[rt][gh][h][0], tot[rt][h][0]);
-              if (NB != 1) tot[rt][h][1] = fmaf(s0, acc[rt][gh][h][1], tot[rt][h][1]);
-              tot[rt][h][2] = fmaf(s1, FOLD ? acc[rt][gh][h][2] + cg : acc[rt][gh][h][2], tot[rt][h][2]);
-              if (NB != 1) tot[rt][h][3] = fmaf(s1, acc[rt][gh][h][3], tot[rt][h][3]);
-            }
-          }
-      } else if (FOLD && !ROWFOLD) {  // per-row scale: the groups are summed unscaled
-#pragma unroll
-        for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-          for (int gh = 0; gh < 2; ++gh)
-#pragma unroll
-            for (int h = 0; h < NH; ++h)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) tot[rt][h][i] += acc[rt][gh][h][i];
-      }
-    }
-  }
-}
 
 // Warp owning unit u of a range split [floor(w*U/T), floor((w+1)*U/T)).
 __device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
@@ -781,11 +564,11 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const int nslab = min(SLABS, ks - s0);
     if (ROWFOLD) csum += lds_f32(corrw + (uint32_t)win * 4u);
     if (nslab == SLABS)
-      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(wbase, sbase, xs, corr, nslab,
-                                                                      s0 * kSlabCols, p, g, t, lo, acc, tot);
+      consume_window<true, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(
+          wbase, sbase, xs, corr, nslab, s0 * kSlabCols, p.x, p.K, p.M, g, t, lo, acc, tot);
     else
-      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(wbase, sbase, xs, corr, nslab,
-                                                                       s0 * kSlabCols, p, g, t, lo, acc, tot);
+      consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(
+          wbase, sbase, xs, corr, nslab, s0 * kSlabCols, p.x, p.K, p.M, g, t, lo, acc, tot);
     __syncwarp();  // every lane has read the slot before it is refilled
     issue_one();
 

@@ -109,6 +109,17 @@ constexpr size_t kTpCapacityOffset = 128;
 // waits ran out.  Synchronises `stream`.
 int read_device_error(int* code, cudaStream_t stream);
 
+// The one-kernel decode step (w4a16_decode_step.cu): a plan holds the projection tables,
+// tensor maps and the step's scratch for one model on one device.
+struct DecodePlan;
+int decode_plan_create(const w4a16_llama_desc* desc, DecodePlan** out);
+int decode_plan_destroy(DecodePlan* plan);
+int decode_step_launch(DecodePlan* plan, const long long* token, const long long* pos, void* k_cache,
+                       void* v_cache, float* logits, cudaStream_t stream);
+int read_decode_step_error(int* code, cudaStream_t stream);
+int decode_plan_timeline(DecodePlan* plan, int enable, unsigned long long* host, size_t capacity,
+                         size_t* count, cudaStream_t stream);
+
 // Thread-local description of the last failure, for w4a16_last_error_string().
 void set_error(const char* fmt, ...);
 const char* last_error();

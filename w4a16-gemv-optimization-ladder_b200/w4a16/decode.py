@@ -20,6 +20,7 @@ same GEMVs with the norms, rotary, cache write, attention (SDPA) and SwiGLU as t
 ops in between; `dense=True` builds the model with fp16 weights on cuBLAS (`F.linear`)
 and the torch ops, for comparison.
 """
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -86,16 +87,128 @@ class _Proj:
                       out_dtype=out.dtype)
 
 
+def interleave_gate_up(w, inter):
+    """[gate (inter rows) | up (inter rows)] -> blocks of 8 gate rows followed by the
+    matching 8 up rows (the layout the one-kernel step applies SwiGLU to in its epilogue)."""
+    rest = w.shape[1:]
+    return w.view(2, inter // 8, 8, *rest).transpose(0, 1).reshape(2 * inter, *rest).contiguous()
+
+
+def split_gate_up(v, inter, interleaved):
+    """(gate, up) halves of a gate|up projection output in either row layout."""
+    if not interleaved:
+        return v[:inter], v[inter:]
+    b = v.view(inter // 8, 2, 8)
+    return b[:, 0].reshape(inter), b[:, 1].reshape(inter)
+
+
+class _G128Weight(ctypes.Structure):
+    _fields_ = [("packed", ctypes.c_void_p), ("scale", ctypes.c_void_p)]
+
+
+class _LlamaDesc(ctypes.Structure):
+    """w4a16_llama_desc of include/w4a16_b200.h."""
+    _fields_ = [("layers", ctypes.c_int), ("hidden", ctypes.c_int), ("intermediate", ctypes.c_int),
+                ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("max_len", ctypes.c_int), ("eps", ctypes.c_float),
+                ("qkv", ctypes.POINTER(_G128Weight)), ("o", ctypes.POINTER(_G128Weight)),
+                ("gate_up", ctypes.POINTER(_G128Weight)), ("down", ctypes.POINTER(_G128Weight)),
+                ("norm_attn", ctypes.POINTER(ctypes.c_void_p)), ("norm_mlp", ctypes.POINTER(ctypes.c_void_p)),
+                ("lm_head", _G128Weight), ("norm_final", ctypes.c_void_p), ("embed", ctypes.c_void_p),
+                ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p), ("gate_up_interleaved", ctypes.c_int)]
+
+
+class DecodePlan:
+    """The one-kernel decode step of the C ABI (w4a16_decode_plan_create / w4a16_decode_step)
+    for a decoder's int4 weights: every layer and the head in one persistent launch."""
+
+    def __init__(self, dec):
+        from . import _lib
+
+        cfg = dec.cfg
+        self.lib = _lib.lib()
+        self._check = _lib.check
+        self.device = dec.device
+
+        def wt(p):
+            return _G128Weight(p.packed.data_ptr(), p.scale.data_ptr())
+
+        L = cfg.layers
+        arrs = {name: (_G128Weight * L)(*[wt(layer[name]) for layer in dec.layers])
+                for name in ("qkv", "o", "gu", "down")}
+        na = (ctypes.c_void_p * L)(*[layer["norm_attn"].data_ptr() for layer in dec.layers])
+        nm = (ctypes.c_void_p * L)(*[layer["norm_mlp"].data_ptr() for layer in dec.layers])
+        d = _LlamaDesc(L, cfg.hidden, cfg.intermediate, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.vocab,
+                       cfg.max_len, cfg.eps, arrs["qkv"], arrs["o"], arrs["gu"], arrs["down"], na, nm,
+                       wt(dec.lm_head), dec.norm_final.data_ptr(), dec.embed.data_ptr(), dec.cos.data_ptr(),
+                       dec.sin.data_ptr(), 8 if dec.gu_interleaved else 0)
+        self.plan = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            self._check(self.lib.w4a16_decode_plan_create(ctypes.byref(d), ctypes.byref(self.plan)),
+                        "w4a16_decode_plan_create")
+
+    def step(self, token, pos, k_cache, v_cache, logits):
+        """Launch one step on the current stream (token, pos: device int64 [1])."""
+        with torch.cuda.device(self.device):
+            st = self.lib.w4a16_decode_step(self.plan, ctypes.c_void_p(token.data_ptr()),
+                                            ctypes.c_void_p(pos.data_ptr()), ctypes.c_void_p(k_cache.data_ptr()),
+                                            ctypes.c_void_p(v_cache.data_ptr()), ctypes.c_void_p(logits.data_ptr()),
+                                            K._stream(self.device))
+        self._check(st, "w4a16_decode_step")
+        return logits
+
+    def timeline(self, enable=True):
+        """Start (enable=True) recording the per-CTA %globaltimer timeline of each step, or
+        stop it.  Returns the number of entries a record holds."""
+        n = ctypes.c_size_t(0)
+        with torch.cuda.device(self.device):
+            self._check(self.lib.w4a16_decode_plan_timeline(self.plan, int(enable), None, 0, ctypes.byref(n),
+                                                            K._stream(self.device)), "w4a16_decode_plan_timeline")
+        return n.value
+
+    def read_timeline(self, grid):
+        """The last step's record as an int64 tensor [3 * (barriers + 1), grid] (ns): rows
+        3b, 3b + 1, 3b + 2 are barrier b's arrival, departure and the next phase's staged
+        input (b = 0: start, end, first phase staged)."""
+        import numpy as np
+
+        n = self.timeline(True)
+        buf = np.zeros(n, dtype=np.uint64)
+        with torch.cuda.device(self.device):
+            self._check(self.lib.w4a16_decode_plan_timeline(self.plan, 1, ctypes.c_void_p(buf.ctypes.data), n, None,
+                                                            K._stream(self.device)), "w4a16_decode_plan_timeline")
+        return torch.from_numpy(buf.astype(np.int64)).view(-1, grid)
+
+    def close(self):
+        if self.plan:
+            self.lib.w4a16_decode_plan_destroy(self.plan)
+            self.plan = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class W4A16LlamaDecoder:
-    """Random-init Llama decoder for one-token steps (batch 1) over a static KV cache."""
+    """Random-init Llama decoder for one-token steps (batch 1) over a static KV cache.
+
+    fused: the step as the fused GEMV / attention kernels (one launch each, ~5 per layer);
+    persistent: the whole step as one persistent kernel (DecodePlan), int4 weights only."""
 
     def __init__(self, cfg=LLAMA_3_2_1B, device="cuda", seed=0, dense=False, std=0.02, fused=None,
-                 pdl=None):
+                 pdl=None, persistent=False):
         self.cfg = cfg
         self.dense = dense
-        self.fused = (not dense) if fused is None else bool(fused)
+        self.persistent = bool(persistent)
+        if self.persistent and (dense or cfg.head_dim != 64):
+            raise ValueError("the persistent step needs int4 weights and head_dim 64")
+        self.fused = (not dense and not self.persistent) if fused is None else bool(fused)
         if self.fused and (dense or cfg.head_dim != 64):
             raise ValueError("the fused step needs int4 weights and head_dim 64")
+        # the one-kernel step keeps gate and up rows interleaved by 8 (SwiGLU in the epilogue)
+        self.gu_interleaved = self.persistent
         # chained launches (each kernel starts while the previous one finishes)
         self.pdl = self.fused if pdl is None else bool(pdl) and self.fused
         dev = torch.device(device)
@@ -112,7 +225,7 @@ class W4A16LlamaDecoder:
             self.layers.append(dict(
                 qkv=_Proj(rnd(cfg.qkv_rows, H), dense),
                 o=_Proj(rnd(H, cfg.heads * D), dense),
-                gu=_Proj(rnd(2 * I, H), dense),
+                gu=_Proj(interleave_gate_up(rnd(2 * I, H), I) if self.gu_interleaved else rnd(2 * I, H), dense),
                 down=_Proj(rnd(H, I), dense),
                 norm_attn=torch.ones(H, device=dev),
                 norm_mlp=torch.ones(H, device=dev),
@@ -137,6 +250,7 @@ class W4A16LlamaDecoder:
         self.ws = [K.new_workspace(dev), K.new_workspace(dev)] if self.fused else None
         self.logits = torch.empty(cfg.vocab, dtype=torch.float32, device=dev)
         self.graph = None
+        self.plan = DecodePlan(self) if self.persistent else None
         # greedy generation on the device: the next token and position are written by the
         # graph itself, generated tokens collected in gen_tokens
         self.gen_tokens = torch.zeros(cfg.max_len, dtype=torch.long, device=dev)
@@ -199,6 +313,8 @@ class W4A16LlamaDecoder:
         return self.logits
 
     def _step(self):
+        if self.persistent:
+            return self.plan.step(self.token, self.pos, self.k_cache, self.v_cache, self.logits)
         if self.fused:
             return self._step_fused()
         cfg = self.cfg
@@ -325,8 +441,8 @@ class W4A16LlamaDecoder:
             attn = (att.unsqueeze(1) @ vals).reshape(-1)
             h = h + L["o"].dequantized() @ attn
             x = norm(h, L["norm_mlp"]).half().float()
-            gu = L["gu"].dequantized() @ x
-            a = F.silu(gu[:cfg.intermediate]) * gu[cfg.intermediate:]
+            gate, up = split_gate_up(L["gu"].dequantized() @ x, cfg.intermediate, self.gu_interleaved)
+            a = F.silu(gate) * up
             h = h + L["down"].dequantized() @ a
         return self.lm_head.dequantized() @ norm(h, self.norm_final)
 
@@ -338,7 +454,7 @@ def main(argv=None):
     import json
 
     ap = argparse.ArgumentParser(description=main.__doc__)
-    ap.add_argument("--mode", choices=["fused", "unfused", "dense"], default="fused")
+    ap.add_argument("--mode", choices=["persistent", "fused", "unfused", "dense"], default="persistent")
     ap.add_argument("--no-pdl", action="store_true", help="fused mode without chained launches")
     ap.add_argument("--layers", type=int, default=LLAMA_3_2_1B.layers)
     ap.add_argument("--max-len", type=int, default=LLAMA_3_2_1B.max_len)
@@ -350,7 +466,7 @@ def main(argv=None):
     a = ap.parse_args(argv)
     cfg = LlamaDecodeConfig(layers=a.layers, max_len=a.max_len)
     dec = W4A16LlamaDecoder(cfg, dense=a.mode == "dense", fused=a.mode == "fused",
-                            pdl=False if a.no_pdl else None)
+                            pdl=False if a.no_pdl else None, persistent=a.mode == "persistent")
     pos = cfg.max_len - 1
     dec.fill_cache(pos)
     dec.token.fill_(1)
