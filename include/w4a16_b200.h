@@ -328,7 +328,8 @@ int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int grou
 
 /* Reads and clears the error word that kernels set when a bounded wait runs out
  * (0 = none; 1 = a weight copy did not land in time; 2 = another rank's flag did not
- * arrive in time; 3 = a grid barrier of w4a16_decode_step timed out).  Synchronises `stream`.  A non-zero code means some warps returned
+ * arrive in time; 3 = a grid barrier of w4a16_decode_step timed out; 4 = a decode plan's
+ * shared-memory layout was not aligned, nothing ran).  Synchronises `stream`.  A non-zero code means some warps returned
  * early: their rows of the output are missing, and a split-K workspace they used may hold
  * non-zero counters, so zero-fill again every workspace used since the previous read
  * (w4a16_gemv_noalloc clears its own on every call). */

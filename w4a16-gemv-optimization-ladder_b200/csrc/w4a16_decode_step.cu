@@ -79,7 +79,7 @@ constexpr uint64_t kDsSyncWaitNs = 1000000000ull;   // barriers and tile counter
 constexpr uint64_t kDsDrainWaitNs = 100000000ull;
 
 // Error codes of this kernel (w4a16_read_device_error reports them).
-enum : int { kDsErrStage = 1, kDsErrBarrier = 3 };
+enum : int { kDsErrStage = 1, kDsErrBarrier = 3, kDsErrLayout = 4 };
 
 __device__ int g_ds_error = 0;
 
@@ -146,6 +146,7 @@ struct DsParams {
   int layers, hidden, inter, heads, kv_heads, max_len, splits, nmats, vocab;
   int gu_interleaved;          // gate|up rows interleaved by 8: P.gu holds the activation [inter]
   int kv_off;                  // shared-memory offset (in the x area) of the attention rows
+  int lpart_off, table_off;    // shared-memory offsets (from the x area) of the local partials and table
   int xbytes;                  // shared-memory bytes of the staged vector / attention state
   float eps;
   // optional timeline, [3 * (barriers + 1)][grid] %globaltimer ns per CTA: start, end and
@@ -666,7 +667,8 @@ __global__ void __launch_bounds__(kDsThreads, 1) k_decode_step(const __grid_cons
   const int nmats = P.nmats;
 
   // shared memory: [rings][scales][mbarriers][x staging | attention state: xbytes]
-  // [128 B scratch][group corrections: xbytes / 256 floats][local partial sums]
+  // [128 B scratch][group corrections: kmax / 128 floats, 128-byte padded][local partial
+  // sums][projection table]
   const uint32_t wring = base + (uint32_t)(warp * kDsStages * DsL::kWStride);
   const uint32_t sring = base + (uint32_t)(DsPlanLayout::kScaleOff + warp * kDsStages * DsL::kSStride);
   const uint32_t bar0 = base + (uint32_t)(DsPlanLayout::kBarOff + warp * kDsStages * 8);
@@ -676,9 +678,15 @@ __global__ void __launch_bounds__(kDsThreads, 1) k_decode_step(const __grid_cons
   uint8_t* xsp = sbase_ptr + DsPlanLayout::kXOff;
   float* redp = reinterpret_cast<float*>(xsp + xbytes);
   float* corr_f = redp + 32;
-  float* lpart = corr_f + xbytes / 256;  // [kLocalMaxWindows][16]
+  // [local partials: kLocalMaxWindows x 16 floats][projection table], 128-byte aligned
+  // offsets from the plan (the corrections before them take kmax / 128 floats)
+  float* lpart = reinterpret_cast<float*>(xsp + P.lpart_off);
   // the projection table, copied from global memory: the unit streams read it on every step
-  DsMat* mats = reinterpret_cast<DsMat*>(lpart + kLocalMaxWindows * kMmaRows);
+  DsMat* mats = reinterpret_cast<DsMat*>(xsp + P.table_off);
+  if ((P.table_off | P.lpart_off | P.kv_off | P.xbytes) & 127) {  // the plan keeps them 128-aligned
+    if (threadIdx.x == 0) ds_record_error(kDsErrLayout);
+    return;  // every CTA returns here: no barrier is left waiting
+  }
   for (int i = threadIdx.x; i < nmats * (int)(sizeof(DsMat) / 16); i += blockDim.x)
     reinterpret_cast<uint4*>(mats)[i] = __ldg(reinterpret_cast<const uint4*>(P.mats) + i);
   __shared__ unsigned s_prev;
@@ -994,10 +1002,12 @@ int decode_plan_create(const w4a16_llama_desc* d, DecodePlan** out) {
   const int kv_off = (int)align_up((size_t)(2 * H > attn_state ? 2 * H : attn_state), 128);
   const int kv_end = kv_off + 2 * kAttnSpan * kHeadDim * 2;
   const int xbytes = (int)align_up((size_t)(kmax * 2 > kv_end ? kmax * 2 : kv_end), 128);
-  // [x | attention state][128 B scratch][corrections: xbytes / 256 floats][local partials]
+  // [x | attention state][128 B scratch][corrections: kmax / 128 floats][local partials]
   // [projection table]
-  const int smem = DsPlanLayout::kXOff + xbytes + 128 + xbytes / 64 + kLocalMaxWindows * kMmaRows * 4 +
-                   (4 * L + 1) * (int)sizeof(DsMat) + 1024;
+  const int lpart_off = xbytes + 128 + (int)align_up((size_t)(kmax / 128) * 4, 128);
+  const int table_off = lpart_off + kLocalMaxWindows * kMmaRows * 4;
+  static_assert((kLocalMaxWindows * kMmaRows * 4) % 128 == 0, "table offset alignment");
+  const int smem = DsPlanLayout::kXOff + table_off + (4 * L + 1) * (int)sizeof(DsMat) + 1024;
   if (smem > smem_optin) {
     set_error("decode step needs %d bytes of shared memory, the device allows %d", smem, smem_optin);
     return W4A16_ERR_SHAPE;
@@ -1181,6 +1191,8 @@ int decode_plan_create(const w4a16_llama_desc* d, DecodePlan** out) {
   p.vocab = d->vocab;
   p.gu_interleaved = d->gate_up_interleaved ? 1 : 0;
   p.kv_off = kv_off;
+  p.lpart_off = lpart_off;
+  p.table_off = table_off;
   p.xbytes = xbytes;
   p.eps = d->eps;
   *out = plan;

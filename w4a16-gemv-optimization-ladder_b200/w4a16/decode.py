@@ -95,11 +95,13 @@ def interleave_gate_up(w, inter):
 
 
 def split_gate_up(v, inter, interleaved):
-    """(gate, up) halves of a gate|up projection output in either row layout."""
+    """(gate, up) halves of a gate|up projection output (or of its weight rows) in either
+    row layout."""
     if not interleaved:
         return v[:inter], v[inter:]
-    b = v.view(inter // 8, 2, 8)
-    return b[:, 0].reshape(inter), b[:, 1].reshape(inter)
+    rest = v.shape[1:]
+    b = v.view(inter // 8, 2, 8, *rest)
+    return b[:, 0].reshape(inter, *rest), b[:, 1].reshape(inter, *rest)
 
 
 class _G128Weight(ctypes.Structure):
@@ -198,7 +200,11 @@ class W4A16LlamaDecoder:
     persistent: the whole step as one persistent kernel (DecodePlan), int4 weights only."""
 
     def __init__(self, cfg=LLAMA_3_2_1B, device="cuda", seed=0, dense=False, std=0.02, fused=None,
-                 pdl=None, persistent=False):
+                 pdl=None, persistent=False, weights=None):
+        """weights: None for random N(0, std) projections and unit norms, or a dict with
+        embed [vocab, hidden], lm_head (None: tied to embed), norm_final [hidden] and
+        layers: a list of dicts with q, k, v, o, gate, up, down (the nn.Linear weight
+        matrices, [out, in]) and norm_attn, norm_mlp (see from_hf)."""
         self.cfg = cfg
         self.dense = dense
         self.persistent = bool(persistent)
@@ -219,19 +225,40 @@ class W4A16LlamaDecoder:
         def rnd(*shape):
             return (torch.randn(*shape, device=dev, generator=g) * std).half()
 
-        self.embed = rnd(cfg.vocab, H)
+        def gate_up(w):
+            return interleave_gate_up(w, I) if self.gu_interleaved else w
+
         self.layers = []
-        for _ in range(cfg.layers):
-            self.layers.append(dict(
-                qkv=_Proj(rnd(cfg.qkv_rows, H), dense),
-                o=_Proj(rnd(H, cfg.heads * D), dense),
-                gu=_Proj(interleave_gate_up(rnd(2 * I, H), I) if self.gu_interleaved else rnd(2 * I, H), dense),
-                down=_Proj(rnd(H, I), dense),
-                norm_attn=torch.ones(H, device=dev),
-                norm_mlp=torch.ones(H, device=dev),
-            ))
-        self.norm_final = torch.ones(H, device=dev)
-        self.lm_head = _Proj(self.embed, dense)  # tied to the embedding, as in Llama-3.2-1B
+        if weights is None:
+            self.embed = rnd(cfg.vocab, H)
+            for _ in range(cfg.layers):
+                self.layers.append(dict(
+                    qkv=_Proj(rnd(cfg.qkv_rows, H), dense),
+                    o=_Proj(rnd(H, cfg.heads * D), dense),
+                    gu=_Proj(gate_up(rnd(2 * I, H)), dense),
+                    down=_Proj(rnd(H, I), dense),
+                    norm_attn=torch.ones(H, device=dev),
+                    norm_mlp=torch.ones(H, device=dev),
+                ))
+            self.norm_final = torch.ones(H, device=dev)
+            self.lm_head = _Proj(self.embed, dense)  # tied to the embedding, as in Llama-3.2-1B
+        else:
+            def t(x):
+                return x.detach().to(dev).float().contiguous()
+
+            self.embed = t(weights["embed"]).half()
+            for lw in weights["layers"]:
+                self.layers.append(dict(
+                    qkv=_Proj(torch.cat([t(lw["q"]), t(lw["k"]), t(lw["v"])]), dense),
+                    o=_Proj(t(lw["o"]), dense),
+                    gu=_Proj(gate_up(torch.cat([t(lw["gate"]), t(lw["up"])])), dense),
+                    down=_Proj(t(lw["down"]), dense),
+                    norm_attn=t(lw["norm_attn"]),
+                    norm_mlp=t(lw["norm_mlp"]),
+                ))
+            self.norm_final = t(weights["norm_final"])
+            head = weights.get("lm_head")
+            self.lm_head = _Proj(self.embed if head is None else t(head), dense)
         # rotary tables (Llama's rotate-half convention)
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=dev).float() / D))
         ang = torch.arange(cfg.max_len, device=dev).float()[:, None] * inv[None, :]
@@ -258,6 +285,31 @@ class W4A16LlamaDecoder:
         self.gen_graph = None
 
     # ------------------------------------------------------------------ pieces
+
+    @classmethod
+    def from_hf(cls, model, device="cuda", max_len=512, **kw):
+        """A decoder with the weights of a Hugging Face LlamaForCausalLM (default rotary,
+        head_dim 64): every Linear is quantised to int4 with group-128 scales here (the
+        model's own weights are left untouched)."""
+        c = model.config
+        head_dim = getattr(c, "head_dim", None) or c.hidden_size // c.num_attention_heads
+        cfg = LlamaDecodeConfig(hidden=c.hidden_size, intermediate=c.intermediate_size,
+                                layers=c.num_hidden_layers, heads=c.num_attention_heads,
+                                kv_heads=c.num_key_value_heads, head_dim=head_dim, vocab=c.vocab_size,
+                                rope_theta=float(getattr(c, "rope_theta", None)
+                                                 or c.rope_parameters["rope_theta"]),
+                                eps=c.rms_norm_eps, max_len=max_len)
+        m = model.model
+        layers = []
+        for lyr in m.layers:
+            a, f = lyr.self_attn, lyr.mlp
+            layers.append(dict(q=a.q_proj.weight, k=a.k_proj.weight, v=a.v_proj.weight, o=a.o_proj.weight,
+                               gate=f.gate_proj.weight, up=f.up_proj.weight, down=f.down_proj.weight,
+                               norm_attn=lyr.input_layernorm.weight, norm_mlp=lyr.post_attention_layernorm.weight))
+        tied = model.lm_head.weight.data_ptr() == m.embed_tokens.weight.data_ptr()
+        weights = dict(embed=m.embed_tokens.weight, norm_final=m.norm.weight, layers=layers,
+                       lm_head=None if tied else model.lm_head.weight)
+        return cls(cfg, device=device, weights=weights, **kw)
 
     def weight_bytes(self):
         per = sum(p.bytes() for L in self.layers for p in (L["qkv"], L["o"], L["gu"], L["down"]))
