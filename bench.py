@@ -644,15 +644,18 @@ def decode_step_times(dev, stream, reps=200):
     """Decode step of the random-init Llama-3.2-1B architecture (16 layers, hidden 2048,
     GQA 32/8, SwiGLU 8192, vocab 128256, tied head), batch 1, KV length 512, replayed
     from one CUDA graph: int4 group-128 weights with the fused norm / attention / SwiGLU
-    kernels (chained launches, and not chained), the same GEMVs with torch ops in
-    between, and dense fp16 on cuBLAS."""
+    kernels (chained launches, and not chained), the whole step as one persistent kernel
+    (w4a16_decode_step), the same GEMVs with torch ops in between, and dense fp16 on
+    cuBLAS."""
     from w4a16.decode import LLAMA_3_2_1B, W4A16LlamaDecoder
     out = {}
-    variants = (("decode_step_us", False, True, True), ("decode_step_us_no_pdl", False, True, False),
-                ("decode_step_us_unfused", False, False, False),
-                ("decode_step_us_fp16_cublas", True, False, False))
-    for name, dense, fused, pdl in variants:
-        dec = W4A16LlamaDecoder(LLAMA_3_2_1B, device=dev, seed=0, dense=dense, fused=fused, pdl=pdl)
+    variants = (("decode_step_us", False, True, True, False), ("decode_step_us_no_pdl", False, True, False, False),
+                ("decode_step_us_one_kernel", False, False, False, True),
+                ("decode_step_us_unfused", False, False, False, False),
+                ("decode_step_us_fp16_cublas", True, False, False, False))
+    for name, dense, fused, pdl, persistent in variants:
+        dec = W4A16LlamaDecoder(LLAMA_3_2_1B, device=dev, seed=0, dense=dense, fused=fused, pdl=pdl,
+                                persistent=persistent)
         dec.fill_cache(LLAMA_3_2_1B.max_len - 1)
         dec.capture()
         dec.token.fill_(1)

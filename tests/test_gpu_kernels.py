@@ -251,6 +251,21 @@ def test_batched_vs_oracle(batch, group):
     assert_close(y.cpu(), ref, what=f"batch {batch}")
 
 
+@pytest.mark.parametrize("rows,batch,group,sdt", [(128256, 16, 128, torch.float32), (14208, 12, 0, torch.float32),
+                                                  (20000, 16, 128, torch.float16), (128256, 4, 128, torch.float32)])
+def test_batched_many_tiles_vs_oracle(rows, batch, group, sdt):
+    # 9..16 activation rows on a matrix of many 32-row tiles take the wide geometry (6 warps,
+    # 32-row tiles; 14208 rows is the smallest that does on 148 SMs), the ragged last tile
+    # included (20000 = 625 x 32)
+    w, _ = _weights(rows, 2048, seed=rows + batch)
+    x = torch.randn(batch, 2048, device=DEV).half()
+    packed, scale = K.quantize_pack(w, group=group, scale_dtype=sdt)
+    del w
+    y = K.gemv(packed, scale, x, group=group)
+    ref = c_oracle.gemv(packed.cpu().numpy(), scale.float().cpu().numpy(), x.cpu().numpy(), group=group)
+    assert_close(y.cpu(), ref, what=f"{rows} rows, batch {batch}")
+
+
 @pytest.mark.parametrize("group", [0, 128])
 def test_fp16_scales_and_fp16_bias_epilogue(group):
     w, x = _weights(4100, 4096, seed=11)

@@ -875,10 +875,32 @@ constexpr int kSlabs = W4A16_TMA_SLABS;
 constexpr int kRT = W4A16_TMA_RT;
 constexpr int kTileRows = kMmaRows * kRT;
 
-template <int GS, typename ST>
+// CTA geometry.  The default: 12 warps, 16-row tiles.  WIDE (9..16 activation rows on a
+// matrix of many tiles): every activation fragment a lane loads (from L1: the batch does not
+// fit shared memory beside the rings) feeds RT = 2 row blocks, halving the activation
+// traffic per weight byte that made the L1 pipe the limiter (lm_head-sized matrices at
+// batch 16: 161 -> 116 us); 6 warps with 32-row stages keep the same bytes in flight.  Fewer
+// warps and tiles lose on small matrices, which keep the default.
+#ifndef W4A16_BATCH_WARPS
+#define W4A16_BATCH_WARPS 6
+#endif
+#ifndef W4A16_BATCH_RT
+#define W4A16_BATCH_RT 2
+#endif
+template <bool WIDE>
+struct Geometry {
+  static constexpr int kW = WIDE ? W4A16_BATCH_WARPS : kWarps;
+  static constexpr int kS = kStages;
+  static constexpr int kR = WIDE ? W4A16_BATCH_RT : kRT;
+  static constexpr int kTile = kMmaRows * kR;
+};
+constexpr int kMaxTileRows = kMmaRows * (W4A16_BATCH_RT > W4A16_TMA_RT ? W4A16_BATCH_RT : W4A16_TMA_RT);
+
+template <int GS, typename ST, bool WIDE = false>
 constexpr int tma_smem_bytes() {
-  using L = StageLayout<kSlabs, kRT, GS, ST>;
-  return SmemPlan<kWarps, kStages, L>::kBytes;
+  using G = Geometry<WIDE>;
+  using L = StageLayout<kSlabs, G::kR, GS, ST>;
+  return SmemPlan<G::kW, G::kS, L>::kBytes;
 }
 
 // Shared memory after the weight/scale rings (the kernel's layout): the staged vector,
@@ -891,11 +913,16 @@ int tail_smem_bytes(int K) {
   return (XM != kXGlobal ? K * 2 : 0) + (NB == 1 ? 128 : 0) + corr;
 }
 
-template <int PACK, int GS, typename ST, int NB, typename OT, int XM, bool TP = false>
+template <int PACK, int GS, typename ST, int NB, typename OT, int XM, bool TP = false, bool WIDE = false>
 int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
+  using G = Geometry<WIDE>;
+  constexpr int kWarps = G::kW;      // this launch's geometry (shadows the batch-1 defaults)
+  constexpr int kStages = G::kS;
+  constexpr int kRT = G::kR;
+  constexpr int kTileRows = G::kTile;
   using L = StageLayout<kSlabs, kRT, GS, ST>;
   auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM, TP>;
-  const int smem_base = tma_smem_bytes<GS, ST>() + tail_smem_bytes<PACK, NB, XM>(p.K);
+  const int smem_base = tma_smem_bytes<GS, ST, WIDE>() + tail_smem_bytes<PACK, NB, XM>(p.K);
   int smem = smem_base;
   if (smem > di.smem_optin) {
     set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
@@ -1085,6 +1112,9 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
     return launch_tma<PACK, GS, ST, 1, OT, kXGlobal>(p, x, M, y, di, dev);
   }
   if (M <= 8) return launch_tma<PACK, GS, ST, 8, OT, kXGlobal>(p, x, M, y, di, dev);
+  // many 32-row tiles (at least three per SM for every warp pair): the wide geometry
+  if ((long long)(p.N + 2 * kMmaRows - 1) / (2 * kMmaRows) >= 3LL * di.sms)
+    return launch_tma<PACK, GS, ST, 16, OT, kXGlobal, false, true>(p, x, M, y, di, dev);
   return launch_tma<PACK, GS, ST, 16, OT, kXGlobal>(p, x, M, y, di, dev);
   }
 }
@@ -1118,7 +1148,7 @@ size_t gemv_counter_bytes() { return kCounterBytes; }
 size_t gemv_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const int mc = M < kMaxBatchPerPass ? M : kMaxBatchPerPass;
-  return kCounterBytes + (size_t)kMaxWarps * 2 * mc * kTileRows * 4;
+  return kCounterBytes + (size_t)kMaxWarps * 2 * mc * kMaxTileRows * 4;
 }
 
 int launch_gemv(const GemvProblem& p) {
