@@ -266,6 +266,18 @@ def test_batched_many_tiles_vs_oracle(rows, batch, group, sdt):
     assert_close(y.cpu(), ref, what=f"{rows} rows, batch {batch}")
 
 
+@pytest.mark.parametrize("rows,cols,group", [(4096, 14336, 128), (1000, 18432, 0), (3000, 12288, 128),
+                                             (2048, 11264, 128)])
+def test_long_rows_vs_oracle(rows, cols, group):
+    # one activation vector too long to sit beside twelve warps' rings: staged beside nine
+    # (Llama-3-8B's down projection is 4096 x 14336)
+    w, x = _weights(rows, cols, seed=rows + cols)
+    packed, scale = K.quantize_pack(w, group=group)
+    y = K.gemv(packed, scale, x, group=group)
+    ref = c_oracle.gemv(packed.cpu().numpy(), scale.cpu().numpy(), x.cpu().numpy(), group=group)
+    assert_close(y.cpu(), ref, what=f"{rows}x{cols}")
+
+
 @pytest.mark.parametrize("group", [0, 128])
 def test_fp16_scales_and_fp16_bias_epilogue(group):
     w, x = _weights(4100, 4096, seed=11)

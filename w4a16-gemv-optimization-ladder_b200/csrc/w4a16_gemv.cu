@@ -144,7 +144,7 @@ enum XMode : int { kXGlobal = 0, kXCopy = 1, kXRmsNorm = 2, kXSwiGlu = 3 };
 enum Sched : int { kSchedStreamK = 0, kSchedStatic = 1, kSchedDynamic = 2, kSchedLocal = 3 };
 
 // 8-element chunks of the staged vector per thread (K <= kStageChunks * 8 * threads).
-constexpr int kStageChunks = 6;
+constexpr int kStageChunks = 8;
 
 // Units one CTA can hold under kSchedLocal, and the shared memory of their partial sums.
 template <int WARPS, int STAGES, int ROWS>
@@ -887,18 +887,25 @@ constexpr int kTileRows = kMmaRows * kRT;
 #ifndef W4A16_BATCH_RT
 #define W4A16_BATCH_RT 2
 #endif
-template <bool WIDE>
+// LONG (one activation vector whose length does not fit shared memory beside 12 warps'
+// rings): 9 warps, so that the vector is still staged in shared memory (Llama-3-8B's down
+// projection, 14336 columns; its fragments otherwise come from L1 one by one).
+#ifndef W4A16_LONGK_WARPS
+#define W4A16_LONGK_WARPS 9
+#endif
+enum GeometryKind : int { kGeoDefault = 0, kGeoWide = 1, kGeoLong = 2 };
+template <int GEO>
 struct Geometry {
-  static constexpr int kW = WIDE ? W4A16_BATCH_WARPS : kWarps;
+  static constexpr int kW = GEO == kGeoWide ? W4A16_BATCH_WARPS : GEO == kGeoLong ? W4A16_LONGK_WARPS : kWarps;
   static constexpr int kS = kStages;
-  static constexpr int kR = WIDE ? W4A16_BATCH_RT : kRT;
+  static constexpr int kR = GEO == kGeoWide ? W4A16_BATCH_RT : kRT;
   static constexpr int kTile = kMmaRows * kR;
 };
 constexpr int kMaxTileRows = kMmaRows * (W4A16_BATCH_RT > W4A16_TMA_RT ? W4A16_BATCH_RT : W4A16_TMA_RT);
 
-template <int GS, typename ST, bool WIDE = false>
+template <int GS, typename ST, int GEO = kGeoDefault>
 constexpr int tma_smem_bytes() {
-  using G = Geometry<WIDE>;
+  using G = Geometry<GEO>;
   using L = StageLayout<kSlabs, G::kR, GS, ST>;
   return SmemPlan<G::kW, G::kS, L>::kBytes;
 }
@@ -913,16 +920,16 @@ int tail_smem_bytes(int K) {
   return (XM != kXGlobal ? K * 2 : 0) + (NB == 1 ? 128 : 0) + corr;
 }
 
-template <int PACK, int GS, typename ST, int NB, typename OT, int XM, bool TP = false, bool WIDE = false>
+template <int PACK, int GS, typename ST, int NB, typename OT, int XM, bool TP = false, int GEO = kGeoDefault>
 int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const DeviceInfo& di, int dev) {
-  using G = Geometry<WIDE>;
+  using G = Geometry<GEO>;
   constexpr int kWarps = G::kW;      // this launch's geometry (shadows the batch-1 defaults)
   constexpr int kStages = G::kS;
   constexpr int kRT = G::kR;
   constexpr int kTileRows = G::kTile;
   using L = StageLayout<kSlabs, kRT, GS, ST>;
   auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM, TP>;
-  const int smem_base = tma_smem_bytes<GS, ST, WIDE>() + tail_smem_bytes<PACK, NB, XM>(p.K);
+  const int smem_base = tma_smem_bytes<GS, ST, GEO>() + tail_smem_bytes<PACK, NB, XM>(p.K);
   int smem = smem_base;
   if (smem > di.smem_optin) {
     set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
@@ -1109,12 +1116,15 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
       }
     }
     if (xs_fits) return launch_tma<PACK, GS, ST, 1, OT, kXCopy>(p, x, M, y, di, dev);
+    if (tma_smem_bytes<GS, ST, kGeoLong>() + tail_smem_bytes<PACK, 1, kXCopy>(p.K) <= di.smem_optin &&
+        p.K <= kStageChunks * 8 * Geometry<kGeoLong>::kW * 32)
+      return launch_tma<PACK, GS, ST, 1, OT, kXCopy, false, kGeoLong>(p, x, M, y, di, dev);
     return launch_tma<PACK, GS, ST, 1, OT, kXGlobal>(p, x, M, y, di, dev);
   }
   if (M <= 8) return launch_tma<PACK, GS, ST, 8, OT, kXGlobal>(p, x, M, y, di, dev);
   // many 32-row tiles (at least three per SM for every warp pair): the wide geometry
   if ((long long)(p.N + 2 * kMmaRows - 1) / (2 * kMmaRows) >= 3LL * di.sms)
-    return launch_tma<PACK, GS, ST, 16, OT, kXGlobal, false, true>(p, x, M, y, di, dev);
+    return launch_tma<PACK, GS, ST, 16, OT, kXGlobal, false, kGeoWide>(p, x, M, y, di, dev);
   return launch_tma<PACK, GS, ST, 16, OT, kXGlobal>(p, x, M, y, di, dev);
   }
 }
