@@ -120,3 +120,44 @@ def gemv(q, scale, x, group=0):
 def gemv_packed(packed, scale, x, group=0, interleaved=True):
     """gemv() starting from packed bytes."""
     return gemv(unpack_int4(packed, interleaved), scale, x, group)
+
+
+def gemv_h2f32(q, scale, x):
+    """The reference's deliberately lossy h2f32 kernel (kernels/w4a16_kernels.cu:161-171),
+    every floating-point operation emulated in its order, so the result is bit-exact.
+
+    q: signed codes [rows, cols] (cols a multiple of 8), scale: fp32 per row, x: fp16.
+    Lane l of a row's warp takes packed words l, l+32, ... in order.  Per word, pairs
+    (2k, 2k+1) run two fp16 chains: even = f16(q0*x0), f16(q2*x2 + even), f16(q4*x4 +
+    even), f16(q6*x6 + even), likewise odd over columns 1,3,5,7 (mul.rn then fma.rn,
+    each rounded once; the float64 intermediates here are exact).  The lane sum is
+    p = p + (f32(even) + f32(odd)) in fp32; then p = p * scale, and the warp's shuffle
+    tree p += shfl_down(p, o) for o = 16, 8, 4, 2, 1 leaves lane 0's value.
+    """
+    q = np.asarray(q)
+    rows, cols = q.shape
+    words = cols // 8
+    qw = q.reshape(rows, words, 8).astype(np.float64)
+    xw = np.asarray(x, dtype=np.float16).astype(np.float64).reshape(words, 8)
+
+    def f16(v):
+        return v.astype(np.float16).astype(np.float64)
+
+    with np.errstate(over="ignore", invalid="ignore"):
+        chains = []
+        for c0 in (0, 1):
+            t = f16(qw[:, :, c0] * xw[:, c0])
+            for c in (c0 + 2, c0 + 4, c0 + 6):
+                t = f16(qw[:, :, c] * xw[:, c] + t)
+            chains.append(t.astype(np.float32))
+        wsum = chains[0] + chains[1]                      # float32 add
+        lanes = np.zeros((rows, 32), dtype=np.float32)
+        for g0 in range(0, words, 32):
+            n = min(32, words - g0)
+            lanes[:, :n] = lanes[:, :n] + wsum[:, g0:g0 + n]
+        lanes = lanes * np.asarray(scale, dtype=np.float32)[:, None]
+        for o in (16, 8, 4, 2, 1):
+            shifted = lanes.copy()
+            shifted[:, :32 - o] = lanes[:, o:]            # shfl_down keeps its own value past lane 31-o
+            lanes = lanes + shifted
+    return lanes[:, 0]

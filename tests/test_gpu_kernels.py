@@ -99,6 +99,25 @@ def test_h2f32_is_documented_lossy(shape):
     assert not torch.allclose(out, ref, atol=REF_ATOL), "h2f32 passes the tight tolerance"
 
 
+@pytest.mark.parametrize("rows,cols,vscale", [(4096, 2048, 1.0), (1037, 560, 1.0), (64, 20480, 1.0),
+                                              (300, 4096, 1500.0), (7, 8, 1.0)],
+                         ids=lambda v: str(v))
+def test_h2f32_bit_exact_vs_oracle(rows, cols, vscale):
+    # every fp16 rounding, the per-lane fp32 order and the shuffle tree of the
+    # reference's kernel, emulated; vscale 1500 drives some fp16 sums into overflow (inf)
+    rng = np.random.default_rng(rows + cols)
+    q = rng.integers(-8, 8, size=(rows, cols)).astype(np.int8)
+    x = (rng.standard_normal(cols) * vscale).astype(np.float16)
+    scale = (rng.random(rows) * 0.1 + 0.01).astype(np.float32)
+    packed = K.pack_int4(torch.from_numpy(q)).cuda()
+    out = K.matvec_h2f32(packed, torch.from_numpy(scale).cuda(), torch.from_numpy(x).cuda())
+    want = O.gemv_h2f32(q, scale, x)
+    got = out.cpu().numpy()
+    same = (got == want) | (np.isnan(got) & np.isnan(want))
+    assert same.all(), (f"{(~same).sum()} of {rows} rows differ; first "
+                        f"{np.flatnonzero(~same)[:4].tolist()}: got {got[~same][:4]} want {want[~same][:4]}")
+
+
 def test_marlin_matches_champ_exactly_enough():
     q, scale, vec, _, _ = _setup(8192, 2048)
     out_c = K.matvec_champ(K.pack_int4(q).cuda(), scale, vec)

@@ -114,3 +114,43 @@ def test_oracle_batched_matches_rows():
     packed = O.pack_int4_interleaved(q)
     yc = c_oracle.gemv(packed, s, x, threads=2)
     np.testing.assert_allclose(yc, yb, rtol=1e-6, atol=1e-7)
+
+
+def _h2f32_scalar(q, scale, x):
+    """The reference's k_h2f32 (kernels/w4a16_kernels.cu:161-171) as scalar loops: lane l
+    sums words l, l+32, ...; per word two fp16 chains over the column pairs (mul, then fma
+    rounded once each); fp32 lane sums scaled, then reduced by shfl_down."""
+    rows, cols = q.shape
+    out = []
+    for r in range(rows):
+        lanes = []
+        for lane in range(32):
+            p = np.float32(0)
+            for g in range(lane, cols // 8, 32):
+                t = [None, None]
+                for k in range(4):
+                    for h in (0, 1):
+                        c = 8 * g + 2 * k + h
+                        prod = float(q[r, c]) * float(x[c])
+                        t[h] = np.float16(prod if k == 0 else prod + float(t[h]))
+                p = np.float32(p + np.float32(np.float32(t[0]) + np.float32(t[1])))
+            lanes.append(np.float32(p * scale[r]))
+        for o in (16, 8, 4, 2, 1):
+            lanes = [np.float32(lanes[i] + (lanes[i + o] if i + o < 32 else lanes[i])) for i in range(32)]
+        out.append(lanes[0])
+    return np.array(out, dtype=np.float32)
+
+
+@pytest.mark.parametrize("cols,vscale", [(560, 3.0), (2048, 1.0), (64, 1200.0)])
+def test_h2f32_oracle_matches_scalar_restatement(cols, vscale):
+    rng = np.random.default_rng(cols)
+    q = rng.integers(-8, 8, size=(6, cols))
+    x = (rng.standard_normal(cols) * vscale).astype(np.float16)
+    s = rng.random(6).astype(np.float32)
+    got = O.gemv_h2f32(q, s, x)
+    want = _h2f32_scalar(q, s, x)
+    assert np.array_equal(got, want) or np.array_equal(np.isnan(got), np.isnan(want)) and \
+        np.array_equal(got[~np.isnan(got)], want[~np.isnan(want)])
+    if vscale < 10:  # lossy: fp16 rounding of every product shows against the exact sum
+        exact = (q * x.astype(np.float64)).sum(1) * s
+        assert 0 < np.abs(got - exact).max() < 0.5

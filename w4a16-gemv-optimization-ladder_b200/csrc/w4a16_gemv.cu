@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   // fragment is then one shared-memory load.  The staging comes after the first
   // weight copies are in flight.
   constexpr bool XS = XM != kXGlobal;
-  constexpr bool FOLD = W4A16_FOLD && NB == 1 && PACK == W4A16_PACK_INTERLEAVED;
+  constexpr bool FOLD = W4A16_FOLD && NB == 1;
   constexpr bool FOLDLO = FOLD && GS && W4A16_FOLD_LO;
   constexpr bool ROWFOLD = FOLD && !GS && W4A16_ROW_NORESET;
   using Plan = SmemPlan<WARPS, STAGES, L>;
@@ -306,16 +306,27 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     if (!XS) __syncthreads();
   }
 
-  // FOLD: corr[g] = -72 * (sum of the fp16 activation over columns 8i+2, 8i+3, 8i+6,
-  // 8i+7 of group g) (FOLDLO: minus 1032 * the sum over columns 8i, 8i+1, 8i+4, 8i+5 as
-  // well), summed by the 16 threads holding the group's 16 chunks (a thread's chunks are
-  // warp-uniformly in or out of range: K is a multiple of 256).
+  // FOLD: corr[g] = -72 * (sum of the fp16 activation over the columns whose codes
+  // decode_word_fold leaves biased: 8i+2, 8i+3, 8i+6, 8i+7 of group g for the interleaved
+  // packing, the even columns 8i, 8i+2, 8i+4, 8i+6 for the simple one) (FOLDLO: minus
+  // 1032 * the sum over columns 8i, 8i+1, 8i+4, 8i+5 as well), summed by the 16 threads
+  // holding the group's 16 chunks (a thread's chunks are warp-uniformly in or out of
+  // range: K is a multiple of 256).
   const int nch = p.K >> 3;  // 8-element chunks; thread i takes chunks i, i + blockDim, ...
   float* corr_f = reinterpret_cast<float*>(smem_raw + (corr - smem_addr(smem_raw)));
   auto fold_correction = [&](int c, const uint4& v) {
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
-    float part = (a.x + a.y) + (b.x + b.y);
+    float part;
+    if (PACK == W4A16_PACK_SIMPLE) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+      const float2 c2 = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+      const float2 d2 = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+      part = (a.x + b.x) + (c2.x + d2.x);
+    } else {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+      part = (a.x + a.y) + (b.x + b.y);
+    }
     float part_lo = 0.f;
     if (FOLDLO) {
       const float2 c2 = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
@@ -363,7 +374,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (c < nch) {
           v = ldcg128(p.x + c * 8);
-          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = v;
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = PACK == W4A16_PACK_SIMPLE ? simple_order(v) : v;
         }
         if (FOLD) fold_correction(c, v);
       }
@@ -406,7 +417,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           v.y = pack_half2(a.z * r * ga.z, a.w * r * ga.w);
           v.z = pack_half2(b.x * r * gb.x, b.y * r * gb.y);
           v.w = pack_half2(b.z * r * gb.z, b.w * r * gb.w);
-          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = v;
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = PACK == W4A16_PACK_SIMPLE ? simple_order(v) : v;
         }
         if (FOLD) fold_correction(c, v);
       }
@@ -429,7 +440,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
             pk[i] = pack_half2(g2.x / (1.0f + expf(-g2.x)) * u2.x, g2.y / (1.0f + expf(-g2.y)) * u2.y);
           }
           v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = v;
+          *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = PACK == W4A16_PACK_SIMPLE ? simple_order(v) : v;
         }
         if (FOLD) fold_correction(c, v);
       }
@@ -914,7 +925,7 @@ constexpr int tma_smem_bytes() {
 // a 128-byte scratch, the FOLD corrections; kSchedLocal adds its partial sums.
 template <int PACK, int NB, int XM>
 int tail_smem_bytes(int K) {
-  constexpr bool fold = W4A16_FOLD && NB == 1 && PACK == W4A16_PACK_INTERLEAVED;
+  constexpr bool fold = W4A16_FOLD && NB == 1;
   // group corrections, plus one sum per 1024-column window (read by the per-row kernels)
   const int corr = fold ? ((K / 128 + (K + 1023) / 1024) * 4 + 127) / 128 * 128 : 0;
   return (XM != kXGlobal ? K * 2 : 0) + (NB == 1 ? 128 : 0) + corr;
@@ -1143,6 +1154,13 @@ int run_all(const GemvProblem& p, bool use_tma, const DeviceInfo& di, int dev) {
 }
 
 }  // namespace
+
+int current_sm_count(int* sms) {
+  DeviceInfo di;
+  const int rc = current_device_info(&di, nullptr);
+  if (rc == W4A16_OK) *sms = di.sms;
+  return rc;
+}
 
 void set_error(const char* fmt, ...) {
   va_list ap;

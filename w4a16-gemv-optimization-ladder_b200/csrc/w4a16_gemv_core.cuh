@@ -106,7 +106,7 @@ __device__ __forceinline__ LaneOffsets lane_offsets(int g, int t) {
   return o;
 }
 
-// FOLD (one activation vector, interleaved packing): weights decoded with
+// FOLD (one activation vector): weights decoded with
 // decode_word_fold (or, with FOLD_LO, decode_word_fold_all), leaving a known bias on
 // the codes; corr[group] = -(bias x sum of x over the group's biased columns) cancels it
 // exactly up to fp32 rounding.
@@ -129,7 +129,7 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
   constexpr int NH = BatchCfg<NB>::kHalves;
   constexpr int kGroups = SLABS * 2;
   constexpr bool ROWFOLD = FOLD && !GS && W4A16_ROW_NORESET;
-  static_assert(!FOLD || (NB == 1 && PACK == W4A16_PACK_INTERLEAVED), "FOLD: one vector, interleaved");
+  static_assert(!FOLD || NB == 1, "FOLD: one activation vector");
   static_assert(!FOLDLO || (FOLD && GS), "FOLDLO: group-128 folded decode only");
 #pragma unroll
   for (int sl = 0; sl < SLABS; ++sl) {
@@ -160,7 +160,7 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
           for (int h = 0; h < NH; ++h) {
             xv[h] = XS ? lds128(xwin + ((sl * 2 + gh) * 4 + j) * 64)
                        : load_x<NB>(xg, xk, xm, g, h, col);
-            if (PACK == W4A16_PACK_SIMPLE) xv[h] = simple_order(xv[h]);
+            if (PACK == W4A16_PACK_SIMPLE && !XS) xv[h] = simple_order(xv[h]);  // staged pre-ordered
           }
 #pragma unroll
           for (int rt = 0; rt < RT; ++rt) {

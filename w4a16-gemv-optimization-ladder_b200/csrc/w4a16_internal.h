@@ -122,6 +122,8 @@ int decode_plan_timeline(DecodePlan* plan, int enable, unsigned long long* host,
 
 // Thread-local description of the last failure, for w4a16_last_error_string().
 void set_error(const char* fmt, ...);
+// SM count of the current device (cached per device).
+int current_sm_count(int* sms);
 const char* last_error();
 
 }  // namespace w4a16
