@@ -326,10 +326,24 @@ int w4a16_dequant(const uint8_t* packed, int packing, const void* scale, int sca
 int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int group, int packing,
                         uint8_t* packed, void* scale, int scale_dtype, w4a16_stream_t stream);
 
+/* Many activation rows (prefill) on the tensor cores (tcgen05, accumulators in TMEM):
+ *   y[m][n] = sum_k x[m][k] * w16[n][k] (+ bias[n]),  w16 = fp16(fp32(q[n][k]) * scale(n, k))
+ * w16 is w4a16_dequant's weight, bit for bit, formed in shared memory only; the sums are fp32.
+ * The reference runs every call with more than one activation row through F.linear on fp16
+ * weights (src/w4a16/kernels.py:120-121); this replaces dequantise-then-GEMM for a caller that
+ * keeps no dense copy.  packed uint8 [N][K/2], interleaved packing only, 16-byte aligned;
+ * scale fp32 [N] (group 0) or [N][K/128] (group 128); x fp16 [M][K], 16-byte aligned; bias fp32
+ * [N] or NULL; y fp32 or fp16 [M][N].  K a multiple of 64 (of 128 with group 128), M, N >= 1,
+ * any M and N (ragged tiles are masked).  One CTA per 128 x 128 output tile. */
+int w4a16_gemm(const uint8_t* packed, const float* scale, int group, const void* x,
+               const float* bias, int M, int N, int K, void* y, int out_dtype,
+               w4a16_stream_t stream);
+
 /* Reads and clears the error word that kernels set when a bounded wait runs out
  * (0 = none; 1 = a weight copy did not land in time; 2 = another rank's flag did not
  * arrive in time; 3 = a grid barrier of w4a16_decode_step timed out; 4 = a decode plan's
- * shared-memory layout was not aligned, nothing ran).  Synchronises `stream`.  A non-zero code means some warps returned
+ * shared-memory layout was not aligned, nothing ran; 5 = a pipeline wait of w4a16_gemm
+ * gave up, its output tile is incomplete).  Synchronises `stream`.  A non-zero code means some warps returned
  * early: their rows of the output are missing, and a split-K workspace they used may hold
  * non-zero counters, so zero-fill again every workspace used since the previous read
  * (w4a16_gemv_noalloc clears its own on every call). */

@@ -104,6 +104,30 @@ def test_python_ops_fail_loudly_without_library(monkeypatch, tmp_path):
         _lib.lib.cache_clear()
 
 
+def _gemm(lib, packed=1 << 12, scale=1 << 16, group=0, x=1 << 20, bias=None, M=256, N=256, K=1024,
+          y=1 << 24, odt=0):
+    return lib.w4a16_gemm(ctypes.c_void_p(packed), ctypes.c_void_p(scale), group, ctypes.c_void_p(x),
+                          None if bias is None else ctypes.c_void_p(bias), M, N, K, ctypes.c_void_p(y),
+                          odt, None)
+
+
+def test_gemm_host_validation(lib):
+    # every call fails validation before any CUDA API is reached
+    assert _gemm(lib, odt=3) == -4
+    assert _gemm(lib, group=64) == -4
+    assert _gemm(lib, K=96) == -2                  # K a multiple of 64
+    assert _gemm(lib, K=192, group=128) == -2      # ... of 128 with group-128 scales
+    assert _gemm(lib, M=0) == -2
+    assert _gemm(lib, N=-1) == -2
+    assert _gemm(lib, x=0) == -1
+    assert _gemm(lib, scale=0) == -1
+    assert _gemm(lib, packed=(1 << 12) + 4) == -3  # packed 16-byte aligned (TMA)
+    assert _gemm(lib, x=(1 << 20) + 8) == -3
+    assert _gemm(lib, y=(1 << 24) + 2) == -3       # fp32 output 4-byte aligned
+    assert _gemm(lib, bias=(1 << 16) + 2) == -3
+    assert b"aligned" in lib.w4a16_last_error_string()
+
+
 def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0, flags=0):
     return lib.w4a16_gemv_fused(ctypes.c_void_p(1 << 12), ctypes.c_void_p(1 << 12), 0, 0, prologue,
                                 ctypes.c_void_p(src), ctypes.c_void_p(gamma), 1e-5, rows, cols,

@@ -498,12 +498,43 @@ int w4a16_read_device_error(int* code, w4a16_stream_t stream) {
     set_error("NULL code pointer");
     return W4A16_ERR_NULL;
   }
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   int rc = w4a16::read_device_error(&a, reinterpret_cast<cudaStream_t>(stream));
   if (rc == W4A16_OK) rc = w4a16::read_decode_step_error(&b, reinterpret_cast<cudaStream_t>(stream));
+  if (rc == W4A16_OK) rc = w4a16::read_gemm_error(&c, reinterpret_cast<cudaStream_t>(stream));
   if (rc != W4A16_OK) return rc;
-  *code = a ? a : b;
+  *code = a ? a : b ? b : c;
   return W4A16_OK;
+}
+
+int w4a16_gemm(const uint8_t* packed, const float* scale, int group, const void* x,
+               const float* bias, int M, int N, int K, void* y, int out_dtype,
+               w4a16_stream_t stream) {
+  if (out_dtype != W4A16_DTYPE_F32 && out_dtype != W4A16_DTYPE_F16) {
+    set_error("unknown output dtype code %d", out_dtype);
+    return W4A16_ERR_DTYPE;
+  }
+  if (group != 0 && group != 128) {
+    set_error("group must be 0 (per-row) or 128, got %d", group);
+    return W4A16_ERR_DTYPE;
+  }
+  if (M <= 0 || N <= 0 || K <= 0 || K % 64 != 0 || (group && K % group != 0)) {
+    set_error("bad GEMM shape M=%d N=%d K=%d (K a multiple of %d)", M, N, K, group ? 128 : 64);
+    return W4A16_ERR_SHAPE;
+  }
+  if (!packed || !scale || !x || !y) {
+    set_error("NULL pointer (packed %p, scale %p, x %p, y %p)", (const void*)packed, (const void*)scale,
+              x, y);
+    return W4A16_ERR_NULL;
+  }
+  const size_t osz = out_dtype == W4A16_DTYPE_F32 ? 4 : 2;
+  if (!aligned(packed, 16) || !aligned(x, 16) || !aligned(scale, 4) || !aligned(y, osz) ||
+      (bias && !aligned(bias, 4))) {
+    set_error("misaligned pointer: packed and x need 16 B, scale and bias 4 B, y %zu B", osz);
+    return W4A16_ERR_ALIGN;
+  }
+  return w4a16::launch_gemm(packed, scale, group, x, bias, M, N, K, y, out_dtype,
+                            reinterpret_cast<cudaStream_t>(stream));
 }
 
 int w4a16_decode_plan_create(const w4a16_llama_desc* desc, w4a16_decode_plan* plan) {

@@ -1,0 +1,408 @@
+// W4A16 GEMM for many activation rows (prefill), sm_100a tensor cores (tcgen05, TMEM).
+//
+//   y[m, n] = sum_k x[m, k] * w16[n, k] (+ bias[n]),   w16 = fp16(fp32(q[n, k]) * scale(n, k))
+//
+// w16 is the reference's dequantised weight exactly (`dequant_int4`, the fp16 weight a
+// caller without the dense copy multiplies by; the reference itself runs every call with
+// more than one activation row through F.linear on fp16 weights, src/w4a16/kernels.py:
+// 120-121).  The int4 codes are decoded into shared memory, never into HBM: HBM carries
+// N*K/2 packed bytes + scales + M*K*2 activation bytes + the output, against 2*N*K more
+// written and read again by dequantise-then-GEMM.
+//
+// One CTA computes a 128 (weight rows) x BN (activation rows) tile over all of K:
+//   warp 0       TMA copies per 64-column stage: the activation tile (BN x 64 fp16, 128-byte
+//                swizzle: the tensor core's K-major canonical layout) and the packed weight
+//                tile (128 rows x 32 bytes);
+//   warp 1       allocates BN TMEM columns; one lane issues 4 tcgen05.mma (M=128, N=BN, K=16,
+//                fp16 x fp16 -> fp32 in TMEM) per stage and commits each stage's completion to
+//                the stage's "empty" barrier, the last one to the accumulator barrier;
+//   warps 2..5   decode: thread r of the 128 owns weight row r: it reads its 8 packed words of
+//                the stage, forms w16 (exact codes, one fp32 multiply, one rounding to fp16 as
+//                the reference's dequantisation does) and writes the 16-byte chunks into the
+//                swizzled K-major A tile; then the epilogue: the same thread holds TMEM lane r
+//                (its warp's lane quarter), reads the BN accumulators of its row with
+//                tcgen05.ld, adds the bias and stores y[m, n] (32 consecutive n per warp store).
+// Every barrier wait is bounded (2 s of %globaltimer); a wait that gives up records error 5
+// (w4a16_read_device_error), the CTA stops issuing work, waits (bounded) for the copies and
+// MMAs it has in flight and frees its TMEM.  No cluster, no multicast, no peer memory.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "w4a16_device.cuh"
+#include "w4a16_internal.h"
+
+namespace w4a16 {
+
+namespace {
+
+constexpr int kGmRows = 128;     // weight rows per tile: the MMA's M, TMEM lanes
+constexpr int kGmK = 64;         // columns per stage: one 128-byte swizzle atom of fp16
+constexpr int kGmStages = 4;
+constexpr int kGmWarps = 6;      // 0: copies, 1: TMEM + MMA, 2..5: decode + epilogue
+constexpr int kGmErrWait = 5;    // a pipeline wait gave up
+constexpr uint64_t kGmWaitNs = 2000000000ull;
+
+__device__ int g_gemm_error = 0;
+
+__device__ __forceinline__ void gm_fail() { atomicCAS(&g_gemm_error, 0, kGmErrWait); }
+
+template <int BN>
+struct GmLayout {
+  static constexpr uint32_t kA = kGmRows * kGmK * 2;  // decoded weights, fp16
+  static constexpr uint32_t kB = BN * kGmK * 2;       // activations, fp16
+  static constexpr uint32_t kP = kGmRows * kGmK / 2;  // packed weights
+  static constexpr uint32_t kStage = kA + kB + kP;
+  static_assert(kA % 1024 == 0 && kB % 1024 == 0, "swizzled tiles start on 1024-byte boundaries");
+  static_assert(kStage % 1024 == 0, "stages start on 1024-byte boundaries");
+  // [1024 alignment slack][stages][full, decoded, empty barriers per stage, accumulator
+  // barrier, TMEM address]
+  static constexpr uint32_t kBarOff = kGmStages * kStage;
+  static constexpr uint32_t kBytes = 1024 + kBarOff + (3 * kGmStages + 1) * 8 + 8;
+};
+
+// K-major operand tile with the 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes
+// apart (stride byte offset), the leading byte offset unused by this layout (1), descriptor
+// version 1, layout type 2 (SWIZZLE_128B).  Advancing K by 16 elements inside the atom adds
+// 32 bytes to the start address.
+__device__ __forceinline__ uint64_t gm_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D fp32, A and B fp16, both K-major, N = BN, M = 128.
+template <int BN>
+__device__ __forceinline__ uint32_t gm_idesc() {
+  return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kGmRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void gm_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void gm_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void gm_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void gm_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// 16 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void gm_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+struct GemmParams {
+  const float* scale;  // [N] or [N][K/128]
+  const float* bias;   // [N] or null
+  void* y;             // [M][N] fp32 or fp16
+  int M, N, K, group;
+};
+
+template <int BN, typename OT>
+__global__ void __launch_bounds__(kGmWarps * 32, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap,
+              const GemmParams p) {
+  using L = GmLayout<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  const uint32_t bars = base + L::kBarOff;
+  auto full_bar = [&](int s) { return bars + (uint32_t)s * 8u; };
+  auto dec_bar = [&](int s) { return bars + (uint32_t)(kGmStages + s) * 8u; };
+  auto empty_bar = [&](int s) { return bars + (uint32_t)(2 * kGmStages + s) * 8u; };
+  const uint32_t acc_bar = bars + 3u * kGmStages * 8u;
+  const uint32_t tmem_slot = acc_bar + 8u;
+  auto stage_a = [&](int s) { return base + (uint32_t)s * L::kStage; };
+  auto stage_b = [&](int s) { return stage_a(s) + L::kA; };
+  auto stage_p = [&](int s) { return stage_b(s) + L::kB; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kGmRows;
+  const int m0 = blockIdx.y * BN;
+  const int nk = p.K / kGmK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGmStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(dec_bar(s), 4);
+      mbar_init(empty_bar(s), 1);
+    }
+    mbar_init(acc_bar, 1);
+    mbar_fence_init();
+    tma_prefetch_desc(&xmap);
+    tma_prefetch_desc(&pmap);
+  }
+  if (warp == 1) {  // the whole warp allocates BN columns, then gives up the right to allocate more
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  gm_fence_before();
+  __syncthreads();
+  gm_fence_after();
+  uint32_t tmem_d;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(tmem_d) : "r"(tmem_slot) : "memory");
+
+  if (warp == 0) {
+    if (lane == 0) {  // copies
+      const uint64_t keep = 0, stream_once = l2_policy_evict_first();
+      (void)keep;
+      int issued = 0;
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kGmStages, u = kb / kGmStages;
+        if (u > 0 && !mbar_wait_bounded(empty_bar(s), (u - 1) & 1, kGmWaitNs)) {
+          gm_fail();
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(full_bar(s), L::kB + L::kP);
+        // activations are re-read by every weight-row tile: default L2 policy
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+            "[%0], [%1, {%2, %3}], [%4];" ::"r"(stage_b(s)),
+            "l"(reinterpret_cast<uint64_t>(&xmap)), "r"(kb * kGmK), "r"(m0), "r"(full_bar(s))
+            : "memory");
+        tma_load_2d(stage_p(s), &pmap, kb * (kGmK / 2), n0, full_bar(s), stream_once);
+        ++issued;
+      }
+      // the copies this thread issued have all landed before the CTA can exit
+      for (int kb = issued - kGmStages < 0 ? 0 : issued - kGmStages; kb < issued; ++kb)
+        if (!mbar_wait_bounded(full_bar(kb % kGmStages), (kb / kGmStages) & 1, kGmWaitNs)) gm_fail();
+      (void)ok;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issue
+      const uint32_t idesc = gm_idesc<BN>();
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kGmStages, u = kb / kGmStages;
+        if (!mbar_wait_bounded(full_bar(s), u & 1, kGmWaitNs) ||
+            !mbar_wait_bounded(dec_bar(s), u & 1, kGmWaitNs)) {
+          gm_fail();
+          break;
+        }
+        gm_fence_after();
+        const uint64_t da = gm_desc(stage_a(s)), db = gm_desc(stage_b(s));
+#pragma unroll
+        for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes of K per step: +2 in address units
+          gm_mma(tmem_d, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0);
+        gm_commit(empty_bar(s));
+      }
+      gm_commit(acc_bar);  // every MMA issued above (or none) is complete when this arrives
+    }
+  } else {
+    // decode, then epilogue.  Thread r (0..127) owns weight row r of the tile and TMEM lane r.
+    const int quarter = warp & 3;  // TMEM lane quarter a warp may access
+    const int r = quarter * 32 + lane;
+    const int n = n0 + r;
+    const bool row_in = n < p.N;
+    const int ng = p.group ? p.K / p.group : 1;
+    float sc = row_in ? __ldg(p.scale + (size_t)n * ng) : 0.f;
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kGmStages, u = kb / kGmStages;
+      if (p.group && (kb * kGmK) % p.group == 0 && kb > 0)
+        sc = row_in ? __ldg(p.scale + (size_t)n * ng + (kb * kGmK) / p.group) : 0.f;
+      // the decision to stop is warp-uniform: __syncwarp and tcgen05.ld need every lane
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(full_bar(s), u & 1, kGmWaitNs))) {
+        if (lane == 0) gm_fail();
+        ok = false;
+        break;
+      }
+      const uint4 w0 = lds128(stage_p(s) + (uint32_t)r * 32u);
+      const uint4 w1 = lds128(stage_p(s) + (uint32_t)r * 32u + 16u);
+      const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const uint32_t arow = stage_a(s) + (uint32_t)r * 128u;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // word j: columns 8j..8j+7 of the stage (interleaved packing)
+        uint32_t o[4];
+        decode_word(words[j], o);  // exact codes, pairs (0,1) (2,3) (4,5) (6,7)
+        uint32_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&o[i]));
+          h[i] = pack_half2(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc));
+        }
+        const uint32_t dst = arow + (uint32_t)((j ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(h[0]), "r"(h[1]),
+                     "r"(h[2]), "r"(h[3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();  // the tensor core reads these through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dec_bar(s));
+    }
+    // epilogue
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(acc_bar, 0, kGmWaitNs))) {
+      if (lane == 0) gm_fail();
+      ok = false;
+    }
+    gm_fence_after();
+    if (ok) {
+      const float b = (p.bias && row_in) ? __ldg(p.bias + n) : 0.f;
+      OT* y = static_cast<OT*>(p.y);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        gm_ld16(tmem_d + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+        if (row_in) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int m = m0 + c0 + i;
+            if (m < p.M) y[(size_t)m * p.N + n] = from_f32<OT>(v[i] + b);
+          }
+        }
+      }
+    }
+  }
+  gm_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    gm_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(BN)
+                 : "memory");
+  }
+}
+
+typedef CUresult (*GmEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                               const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+GmEncodeFn gm_encode_fn() {
+  static GmEncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GmEncodeFn>(ptr);
+  });
+  return fn;
+}
+
+template <int BN, typename OT>
+int launch_gemm_bn(const uint8_t* packed, const void* x, const GemmParams& prm, cudaStream_t stream) {
+  using L = GmLayout<BN>;
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  int dev = 0;
+  cudaError_t ae = cudaGetDevice(&dev);
+  if (ae == cudaSuccess && dev < 64 && !(configured.load(std::memory_order_acquire) >> dev & 1ull)) {
+    ae = cudaFuncSetAttribute(k_gemm_tc<BN, OT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)L::kBytes);
+    if (ae == cudaSuccess) configured.fetch_or(1ull << dev, std::memory_order_acq_rel);
+  }
+  if (ae != cudaSuccess || dev >= 64) {
+    set_error("configuring k_gemm_tc (%u bytes of shared memory): %s", L::kBytes,
+              ae != cudaSuccess ? cudaGetErrorString(ae) : "device index out of range");
+    return W4A16_ERR_CUDA;
+  }
+  GmEncodeFn enc = gm_encode_fn();
+  if (!enc) {
+    set_error("cuTensorMapEncodeTiled entry point unavailable");
+    return W4A16_ERR_CUDA;
+  }
+  CUtensorMap xmap, pmap;
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)prm.K, (cuuint64_t)prm.M};
+    const cuuint64_t strides[1] = {(cuuint64_t)prm.K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kGmK, (cuuint32_t)BN};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(x), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled(activations) failed: %d", (int)r);
+      return W4A16_ERR_CUDA;
+    }
+  }
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)(prm.K / 2), (cuuint64_t)prm.N};
+    const cuuint64_t strides[1] = {(cuuint64_t)(prm.K / 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)(kGmK / 2), (cuuint32_t)kGmRows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&pmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(packed), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled(packed weights) failed: %d", (int)r);
+      return W4A16_ERR_CUDA;
+    }
+  }
+  const dim3 grid((prm.N + kGmRows - 1) / kGmRows, (prm.M + BN - 1) / BN);
+  k_gemm_tc<BN, OT><<<grid, kGmWarps * 32, L::kBytes, stream>>>(xmap, pmap, prm);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("k_gemm_tc launch failed: %s", cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  return W4A16_OK;
+}
+
+}  // namespace
+
+int launch_gemm(const uint8_t* packed, const float* scale, int group, const void* x, const float* bias,
+                int M, int N, int K, void* y, int out_dtype, cudaStream_t stream) {
+  GemmParams prm;
+  prm.scale = scale;
+  prm.bias = bias;
+  prm.y = y;
+  prm.M = M;
+  prm.N = N;
+  prm.K = K;
+  prm.group = group;
+  if (out_dtype == W4A16_DTYPE_F32) return launch_gemm_bn<128, float>(packed, x, prm, stream);
+  return launch_gemm_bn<128, __half>(packed, x, prm, stream);
+}
+
+int read_gemm_error(int* code, cudaStream_t stream) {
+  int h = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&h, g_gemm_error, sizeof(int), 0, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess && h != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_gemm_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  }
+  if (e != cudaSuccess) {
+    set_error("reading the GEMM error word: %s", cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  *code = h;
+  return W4A16_OK;
+}
+
+}  // namespace w4a16

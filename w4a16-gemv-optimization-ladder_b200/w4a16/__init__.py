@@ -7,6 +7,7 @@ hand-written sm_100a kernels behind the C ABI of libw4a16_b200.so.
 from .kernels import (
     decode_attention,
     dequant_int4,
+    gemm,
     gemv,
     gemv_rmsnorm,
     gemv_staged,
@@ -46,7 +47,7 @@ __all__ = [
     "dequant_ref", "dequant_ref_group", "W4A16Linear", "replace_linear_with_w4a16",
     # additions
     "gemv", "gemv_staged", "gemv_rmsnorm", "gemv_swiglu", "decode_attention", "new_workspace",
-    "dequant_int4", "quantize_pack", "unpack_int4", "reserve_workspace", "save_quantized",
+    "dequant_int4", "gemm", "quantize_pack", "unpack_int4", "reserve_workspace", "save_quantized",
     "load_quantized",
     "read_device_error",
 ]

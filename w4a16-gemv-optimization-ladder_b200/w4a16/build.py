@@ -22,7 +22,7 @@ LIB_NAME = "libw4a16_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
 SOURCES = ["w4a16_gemv.cu", "w4a16_aux.cu", "w4a16_capi.cu", "w4a16_noalloc.cu", "w4a16_decode.cu",
-           "w4a16_decode_step.cu"]
+           "w4a16_decode_step.cu", "w4a16_gemm.cu"]
 HEADERS = ["w4a16_device.cuh", "w4a16_gemv_core.cuh", "w4a16_internal.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

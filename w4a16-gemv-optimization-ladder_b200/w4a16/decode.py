@@ -499,6 +499,46 @@ class W4A16LlamaDecoder:
         return self.lm_head.dequantized() @ norm(h, self.norm_final)
 
 
+PHASES = ("qkv", "attention", "o", "gate_up", "down")
+
+
+def timeline_summary(dec, layers):
+    """One eager step of the one-kernel decode with its per-CTA %globaltimer record, reduced
+    to where the time goes.  Phase p (five per layer: qkv, attention, o, gate_up, down, then
+    the head) runs from the departure of barrier p (the kernel start for p = 0) to the arrival
+    at barrier p + 1 (the kernel end for the head).  Per phase kind, summed over layers, in µs:
+    work = median over CTAs of the phase's span, wait = median over CTAs of the barrier wait
+    that ends it, staged = median time from a barrier's departure until the next phase's input
+    vector is in shared memory; plus the step's span (start of the first CTA to the end of the
+    last)."""
+    plan = dec.plan
+    nb = 5 * layers
+    grid = plan.timeline(True) // (3 * (nb + 1))
+    dec._step()
+    torch.cuda.synchronize()
+    t = plan.read_timeline(grid).double()
+    plan.timeline(False)
+    start, end = t[0], t[1]
+
+    def dep(b):
+        return start if b == 0 else t[3 * b + 1]
+
+    def arr(b):
+        return end if b == nb + 1 else t[3 * b]
+
+    out = {k: {"work_us": 0.0, "wait_us": 0.0, "staged_us": 0.0} for k in PHASES + ("head",)}
+    for ph in range(nb + 1):
+        kind = "head" if ph == nb else PHASES[ph % 5]
+        out[kind]["work_us"] += float((arr(ph + 1) - dep(ph)).median()) / 1e3
+        out[kind]["staged_us"] += float((t[3 * ph + 2] - dep(ph)).median()) / 1e3
+        if ph < nb:
+            out[kind]["wait_us"] += float((t[3 * (ph + 1) + 1] - t[3 * (ph + 1)]).median()) / 1e3
+    out = {k: {kk: round(vv, 1) for kk, vv in v.items()} for k, v in out.items()}
+    out["span_us"] = round(float(end.max() - start.min()) / 1e3, 1)
+    out["barriers"] = nb
+    return out
+
+
 def main(argv=None):
     """Time one decode step (graph replay, or eager launches) of the Llama-3.2-1B
     architecture: the counterpart of the reference's benchmarks/end_to_end.py."""
@@ -513,6 +553,8 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--eager", action="store_true", help="launch op by op (no CUDA graph)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="persistent mode: record one step's per-CTA timeline and report where its time goes")
     ap.add_argument("--generate", type=int, default=0,
                     help="also generate this many tokens greedily on the device and report tokens/s")
     a = ap.parse_args(argv)
@@ -541,6 +583,10 @@ def main(argv=None):
     res = {"mode": a.mode, "pdl": dec.pdl, "graph": not a.eager, "layers": cfg.layers,
            "kv_len": pos + 1, "step_us": round(us, 2), "weight_bytes": dec.weight_bytes(),
            "weight_gbs": round(dec.weight_bytes() / us / 1e3, 1)}
+    if a.timeline:
+        if a.mode != "persistent":
+            raise SystemExit("--timeline needs --mode persistent")
+        res["timeline"] = timeline_summary(dec, cfg.layers)
     if a.generate:
         n = min(a.generate, cfg.max_len - 1)
         dec.capture_generate()

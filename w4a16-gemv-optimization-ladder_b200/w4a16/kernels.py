@@ -376,6 +376,44 @@ def dequant_int4(packed, scale, group=0, packing="interleaved"):
     return out
 
 
+def gemm(packed, scale, x, *, group=0, bias=None, out_dtype=torch.float32, out=None):
+    """y [M, N] = x [M, K] @ dequant_int4(packed, scale, group).T (+ bias), fp32 sums, on the
+    tensor cores (tcgen05, accumulators in tensor memory); the dequantised weight is formed
+    in shared memory only.  For many activation rows (prefill): the GEMV above is the
+    batch 1..64 path.  Interleaved packing, fp32 scales; K a multiple of 64 (128 with
+    group 128).  Raises RuntimeError on bad input and launches nothing."""
+    _check_packed(packed)
+    n, k = packed.shape[0], packed.shape[1] * 2
+    dev = packed.device
+    _need(isinstance(x, torch.Tensor) and x.device == dev and x.dtype == torch.float16 and x.dim() == 2
+          and x.shape[1] == k and x.is_contiguous() and x.data_ptr() % 16 == 0,
+          f"x must be a contiguous 16-byte aligned fp16 [M, {k}] tensor on the weights' device")
+    _need(packed.data_ptr() % 16 == 0, "packed must be 16-byte aligned")
+    _need(group in (0, GROUP), f"group must be 0 or {GROUP}")
+    want = (n,) if group == 0 else (n, k // GROUP)
+    _need(isinstance(scale, torch.Tensor) and scale.device == dev and scale.dtype == torch.float32
+          and tuple(scale.shape) == want and scale.is_contiguous(),
+          f"scale must be a contiguous float32 {want} tensor on the weights' device")
+    _need(k % (GROUP if group else 64) == 0, f"K={k} must be a multiple of {GROUP if group else 64}")
+    _need(out_dtype in _OUT_DTYPES, "out_dtype must be float32 or float16")
+    if bias is not None:
+        _need(bias.device == dev and bias.dtype == torch.float32 and tuple(bias.shape) == (n,)
+              and bias.is_contiguous(), "bias must be a contiguous float32 [N] tensor")
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype, device=dev)
+    _need(out.dtype == out_dtype and tuple(out.shape) == (m, n) and out.is_contiguous() and out.device == dev,
+          "out must be a contiguous [M, N] tensor of out_dtype on the weights' device")
+    if m == 0:
+        return out
+    with torch.cuda.device(dev):
+        status = _lib.lib().w4a16_gemm(_ptr(packed), _ptr(scale), group, _ptr(x),
+                                       _ptr(bias) if bias is not None else None, m, n, k, _ptr(out),
+                                       _OUT_DTYPES[out_dtype], _stream(dev))
+    _lib.check(status, "w4a16_gemm")
+    return out
+
+
 def quantize_pack(w, group=0, packing="interleaved", scale_dtype=torch.float32):
     """Quantise (symmetric int4, per-row or group-128) and pack on the GPU in one launch.
 

@@ -7,8 +7,11 @@ dtype.  Differences, all opt-in or invisible to callers:
     instead of the dense fp16 fallback the reference used for any batch > 1;
   * bias add and the cast to fp16 happen in the kernel epilogue;
   * scale may be group-128 ([out, in/128]) as well as per-row ([out]);
-  * weight_fp16 may be None (no dense copy kept); larger batches then dequantise to
-    fp16 on the GPU and call a dense GEMM.
+  * weight_fp16 may be None (no dense copy kept); larger batches then run the int4
+    tensor-core GEMM (tcgen05, the dequantised weight formed in shared memory only:
+    the same fp16 weight dequant_int4 gives, fp32 sums), or, for shapes it does not
+    take (K not a multiple of 64 / 128), dequantise to fp16 on the GPU and call a
+    dense GEMM.
 """
 import torch
 import torch.nn as nn
@@ -49,6 +52,13 @@ class W4A16Linear(nn.Module):
             vec = xh[0] if m == 1 else xh
             y = K.gemv(self.packed, self.scale, vec, group=self.group, bias=self.bias_f32,
                        out_dtype=odt)
+            return y.to(x.dtype).view(*lead, self.out_features)
+        if self.dense_weight is None and self.in_features % (GROUP if self.group else 64) == 0:
+            xh = xf if xf.dtype == torch.float16 and xf.is_contiguous() else xf.half().contiguous()
+            odt = torch.float16 if x.dtype == torch.float16 else torch.float32
+            # fp16 scales widen to fp32 exactly: the same dequantised weight either way
+            sc = self.scale if self.scale.dtype == torch.float32 else self.scale.float()
+            y = K.gemm(self.packed, sc, xh, group=self.group, bias=self.bias_f32, out_dtype=odt)
             return y.to(x.dtype).view(*lead, self.out_features)
         if self.dense_weight is not None:
             w = self.dense_weight
