@@ -26,6 +26,8 @@ CASES = [  # M, N, K, group
     (300, 128, 64, 0),
     (512, 4096, 4096, 128),
     (77, 130, 256, 128),
+    (600, 16384, 512, 0),     # 256-row activation tiles (enough tiles for every SM), ragged M
+    (1000, 9500, 1024, 128),  # 256-row tiles, ragged M and N
 ]
 
 

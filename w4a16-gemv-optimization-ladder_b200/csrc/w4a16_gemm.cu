@@ -16,12 +16,17 @@
 //   warp 1       allocates BN TMEM columns; one lane issues 4 tcgen05.mma (M=128, N=BN, K=16,
 //                fp16 x fp16 -> fp32 in TMEM) per stage and commits each stage's completion to
 //                the stage's "empty" barrier, the last one to the accumulator barrier;
-//   warps 2..5   decode: thread r of the 128 owns weight row r: it reads its 8 packed words of
-//                the stage, forms w16 (exact codes, one fp32 multiply, one rounding to fp16 as
-//                the reference's dequantisation does) and writes the 16-byte chunks into the
-//                swizzled K-major A tile; then the epilogue: the same thread holds TMEM lane r
-//                (its warp's lane quarter), reads the BN accumulators of its row with
-//                tcgen05.ld, adds the bias and stores y[m, n] (32 consecutive n per warp store).
+//   warps 2..    G decoder groups of four warps (G = 4 for BN = 256, 3 for 128); group g
+//                decodes stages g, g+G, g+2G, ..., so G stages are decoded at once (one warp's pass over a stage is latency-
+//                bound: barrier test, decode, proxy fence, arrive).  Thread r of a group owns
+//                weight row r: it reads the row's 8 packed words of the stage, forms w16 (exact
+//                codes, one fp32 multiply, one rounding to fp16 as the reference's
+//                dequantisation does) and writes the 16-byte chunks into the swizzled K-major A
+//                tile; scales are fetched one stage of the group ahead.  Then the epilogue: the
+//                thread holds TMEM lane r (its warp's lane quarter), reads its group's quarter of
+//                the row's BN accumulators with tcgen05.ld, adds the bias and stores y[m, n] (32
+//                consecutive n per warp store).
+// BN is 256 when that still gives every SM a tile, else 128.
 // Every barrier wait is bounded (2 s of %globaltimer); a wait that gives up records error 5
 // (w4a16_read_device_error), the CTA stops issuing work, waits (bounded) for the copies and
 // MMAs it has in flight and frees its TMEM.  No cluster, no multicast, no peer memory.
@@ -41,8 +46,16 @@ namespace {
 
 constexpr int kGmRows = 128;     // weight rows per tile: the MMA's M, TMEM lanes
 constexpr int kGmK = 64;         // columns per stage: one 128-byte swizzle atom of fp16
-constexpr int kGmStages = 4;
-constexpr int kGmWarps = 6;      // 0: copies, 1: TMEM + MMA, 2..5: decode + epilogue
+template <int BN>
+constexpr int gm_stages() { return BN == 128 ? 6 : 4; }  // as deep as 227 KB of shared memory allows
+// Decoder groups (stages decoded at once; a group is one warp per TMEM lane quarter).  The
+// stage count is a multiple of the group count, so every ring slot is always decoded by the
+// same group, in order: a group never waits on a slot's next phase before it has seen the
+// current one complete (a parity wait that ran a phase ahead would pass on the one before).
+template <int BN>
+constexpr int gm_groups() { return BN == 128 ? 3 : 4; }
+template <int BN>
+constexpr int gm_warps() { return 2 + 4 * gm_groups<BN>(); }  // 0: copies, 1: TMEM + MMA, rest: decode + epilogue
 constexpr int kGmErrWait = 5;    // a pipeline wait gave up
 constexpr uint64_t kGmWaitNs = 2000000000ull;
 
@@ -52,6 +65,8 @@ __device__ __forceinline__ void gm_fail() { atomicCAS(&g_gemm_error, 0, kGmErrWa
 
 template <int BN>
 struct GmLayout {
+  static constexpr int kStages = gm_stages<BN>();
+  static_assert(kStages % gm_groups<BN>() == 0, "each ring slot belongs to one decoder group");
   static constexpr uint32_t kA = kGmRows * kGmK * 2;  // decoded weights, fp16
   static constexpr uint32_t kB = BN * kGmK * 2;       // activations, fp16
   static constexpr uint32_t kP = kGmRows * kGmK / 2;  // packed weights
@@ -60,8 +75,9 @@ struct GmLayout {
   static_assert(kStage % 1024 == 0, "stages start on 1024-byte boundaries");
   // [1024 alignment slack][stages][full, decoded, empty barriers per stage, accumulator
   // barrier, TMEM address]
-  static constexpr uint32_t kBarOff = kGmStages * kStage;
-  static constexpr uint32_t kBytes = 1024 + kBarOff + (3 * kGmStages + 1) * 8 + 8;
+  static constexpr uint32_t kBarOff = kStages * kStage;
+  static constexpr uint32_t kBytes = 1024 + kBarOff + (3 * kStages + 1) * 8 + 8;
+  static_assert(kBytes <= 232448, "fits the 227 KB of shared memory a CTA may use");
 };
 
 // K-major operand tile with the 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes
@@ -129,7 +145,7 @@ struct GemmParams {
 };
 
 template <int BN, typename OT>
-__global__ void __launch_bounds__(kGmWarps * 32, 1)
+__global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap,
               const GemmParams p) {
   using L = GmLayout<BN>;
@@ -137,9 +153,9 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
   const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
   const uint32_t bars = base + L::kBarOff;
   auto full_bar = [&](int s) { return bars + (uint32_t)s * 8u; };
-  auto dec_bar = [&](int s) { return bars + (uint32_t)(kGmStages + s) * 8u; };
-  auto empty_bar = [&](int s) { return bars + (uint32_t)(2 * kGmStages + s) * 8u; };
-  const uint32_t acc_bar = bars + 3u * kGmStages * 8u;
+  auto dec_bar = [&](int s) { return bars + (uint32_t)(L::kStages + s) * 8u; };
+  auto empty_bar = [&](int s) { return bars + (uint32_t)(2 * L::kStages + s) * 8u; };
+  const uint32_t acc_bar = bars + 3u * L::kStages * 8u;
   const uint32_t tmem_slot = acc_bar + 8u;
   auto stage_a = [&](int s) { return base + (uint32_t)s * L::kStage; };
   auto stage_b = [&](int s) { return stage_a(s) + L::kA; };
@@ -152,9 +168,9 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
   const int nk = p.K / kGmK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGmStages; ++s) {
+    for (int s = 0; s < L::kStages; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(dec_bar(s), 4);
+      mbar_init(dec_bar(s), 4);  // the four warps of the group that decodes the stage
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(acc_bar, 1);
@@ -181,7 +197,7 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
       int issued = 0;
       bool ok = true;
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kGmStages, u = kb / kGmStages;
+        const int s = kb % L::kStages, u = kb / L::kStages;
         if (u > 0 && !mbar_wait_bounded(empty_bar(s), (u - 1) & 1, kGmWaitNs)) {
           gm_fail();
           ok = false;
@@ -196,17 +212,29 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
             : "memory");
         tma_load_2d(stage_p(s), &pmap, kb * (kGmK / 2), n0, full_bar(s), stream_once);
         ++issued;
+        // warm L2 with the tiles of the stage one ring ahead, so that copy is an L2 hit
+        const int kp = kb + L::kStages;
+        if (kp < nk) {
+          asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                           reinterpret_cast<uint64_t>(&xmap)),
+                       "r"(kp * kGmK), "r"(m0)
+                       : "memory");
+          asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                           reinterpret_cast<uint64_t>(&pmap)),
+                       "r"(kp * (kGmK / 2)), "r"(n0)
+                       : "memory");
+        }
       }
       // the copies this thread issued have all landed before the CTA can exit
-      for (int kb = issued - kGmStages < 0 ? 0 : issued - kGmStages; kb < issued; ++kb)
-        if (!mbar_wait_bounded(full_bar(kb % kGmStages), (kb / kGmStages) & 1, kGmWaitNs)) gm_fail();
+      for (int kb = issued - L::kStages < 0 ? 0 : issued - L::kStages; kb < issued; ++kb)
+        if (!mbar_wait_bounded(full_bar(kb % L::kStages), (kb / L::kStages) & 1, kGmWaitNs)) gm_fail();
       (void)ok;
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issue
       const uint32_t idesc = gm_idesc<BN>();
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kGmStages, u = kb / kGmStages;
+        const int s = kb % L::kStages, u = kb / L::kStages;
         if (!mbar_wait_bounded(full_bar(s), u & 1, kGmWaitNs) ||
             !mbar_wait_bounded(dec_bar(s), u & 1, kGmWaitNs)) {
           gm_fail();
@@ -222,18 +250,32 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
       gm_commit(acc_bar);  // every MMA issued above (or none) is complete when this arrives
     }
   } else {
-    // decode, then epilogue.  Thread r (0..127) owns weight row r of the tile and TMEM lane r.
-    const int quarter = warp & 3;  // TMEM lane quarter a warp may access
+    // decode, then epilogue.  Decoder group g (warps 2 + 4g .. 5 + 4g, one per TMEM lane
+    // quarter) decodes the stages kb = g, g + G, g + 2G, ...: G stages are decoded at once,
+    // since one warp's pass over a stage is latency-bound.  Thread r (0..127) of a group owns
+    // weight row r (all 8 packed words of the stage) and, in the epilogue, the 16-column
+    // accumulator chunks g, g + G, ... of TMEM lane r.
+    constexpr int kG = gm_groups<BN>();
+    const int quarter = warp & 3;
+    const int grp = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const int n = n0 + r;
     const bool row_in = n < p.N;
     const int ng = p.group ? p.K / p.group : 1;
-    float sc = row_in ? __ldg(p.scale + (size_t)n * ng) : 0.f;
+    const int kb_per_group = p.group ? p.group / kGmK : nk;  // stages sharing one scale
+    auto scale_of = [&](int kb) {
+      return (row_in && kb < nk) ? __ldg(p.scale + (size_t)n * ng + kb / kb_per_group) : 0.f;
+    };
+    // this group's first stage's scale, and its next stage's already on its way
+    float sc = scale_of(grp);
+    float sc_next = scale_of(grp + kG);
     bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kGmStages, u = kb / kGmStages;
-      if (p.group && (kb * kGmK) % p.group == 0 && kb > 0)
-        sc = row_in ? __ldg(p.scale + (size_t)n * ng + (kb * kGmK) / p.group) : 0.f;
+    for (int kb = grp; kb < nk; kb += kG) {
+      const int s = kb % L::kStages, u = kb / L::kStages;
+      if (kb != grp) {
+        sc = sc_next;
+        sc_next = scale_of(kb + kG);
+      }
       // the decision to stop is warp-uniform: __syncwarp and tcgen05.ld need every lane
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(full_bar(s), u & 1, kGmWaitNs))) {
         if (lane == 0) gm_fail();
@@ -248,15 +290,17 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
       for (int j = 0; j < 8; ++j) {  // word j: columns 8j..8j+7 of the stage (interleaved packing)
         uint32_t o[4];
         decode_word(words[j], o);  // exact codes, pairs (0,1) (2,3) (4,5) (6,7)
-        uint32_t h[4];
+        uint32_t hv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&o[i]));
-          h[i] = pack_half2(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc));
+          // one packed conversion (round to nearest per element, as two separate ones would)
+          const __half2 w2 = __floats2half2_rn(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc));
+          hv[i] = *reinterpret_cast<const uint32_t*>(&w2);
         }
         const uint32_t dst = arow + (uint32_t)((j ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(h[0]), "r"(h[1]),
-                     "r"(h[2]), "r"(h[3])
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(hv[0]), "r"(hv[1]),
+                     "r"(hv[2]), "r"(hv[3])
                      : "memory");
       }
       fence_proxy_async_smem();  // the tensor core reads these through the async proxy
@@ -272,8 +316,9 @@ __global__ void __launch_bounds__(kGmWarps * 32, 1)
     if (ok) {
       const float b = (p.bias && row_in) ? __ldg(p.bias + n) : 0.f;
       OT* y = static_cast<OT*>(p.y);
+      // 16-column chunks of the accumulator dealt round-robin to the groups
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = grp * 16; c0 < BN; c0 += 16 * kG) {
         float v[16];
         gm_ld16(tmem_d + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
         if (row_in) {
@@ -363,7 +408,7 @@ int launch_gemm_bn(const uint8_t* packed, const void* x, const GemmParams& prm, 
     }
   }
   const dim3 grid((prm.N + kGmRows - 1) / kGmRows, (prm.M + BN - 1) / BN);
-  k_gemm_tc<BN, OT><<<grid, kGmWarps * 32, L::kBytes, stream>>>(xmap, pmap, prm);
+  k_gemm_tc<BN, OT><<<grid, gm_warps<BN>() * 32, L::kBytes, stream>>>(xmap, pmap, prm);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("k_gemm_tc launch failed: %s", cudaGetErrorString(e));
@@ -384,8 +429,18 @@ int launch_gemm(const uint8_t* packed, const float* scale, int group, const void
   prm.N = N;
   prm.K = K;
   prm.group = group;
-  if (out_dtype == W4A16_DTYPE_F32) return launch_gemm_bn<128, float>(packed, x, prm, stream);
-  return launch_gemm_bn<128, __half>(packed, x, prm, stream);
+  // 256 activation rows per tile halve the decode work per flop; 128 when the wider tiles
+  // would leave SMs idle
+  int sms = 0;
+  const int rc = current_sm_count(&sms);
+  if (rc != W4A16_OK) return rc;
+  const long long tiles256 = (long long)((N + kGmRows - 1) / kGmRows) * ((M + 255) / 256);
+  const bool wide = M > 128 && tiles256 >= sms;
+  if (out_dtype == W4A16_DTYPE_F32)
+    return wide ? launch_gemm_bn<256, float>(packed, x, prm, stream)
+                : launch_gemm_bn<128, float>(packed, x, prm, stream);
+  return wide ? launch_gemm_bn<256, __half>(packed, x, prm, stream)
+              : launch_gemm_bn<128, __half>(packed, x, prm, stream);
 }
 
 int read_gemm_error(int* code, cudaStream_t stream) {

@@ -14,6 +14,7 @@ times and synchronises; the first launch is the warm-up, so a capture takes
     batch4          lm_head-sized 128256 x 2048 group-128, 4 vectors      (k_gemv_tma, NB 8)
     batch16         lm_head-sized 128256 x 2048 group-128, 16 vectors     (k_gemv_tma, NB 16, 6 warps)
     longk           down-projection-sized 8192 x 14336 group-128, 1 vector (k_gemv_tma, 9 warps)
+    gemm            prefill: 2048 activation rows x 4096 x 4096, group-128 (k_gemm_tc)
 """
 import sys
 
@@ -81,6 +82,15 @@ def case_batch16():
 
 def case_longk():
     _batched(8192, 14336, 1, 6)
+
+
+def case_gemm():
+    w, _ = _weights(4096, 4096, 7)
+    p, s = K.quantize_pack(w, group=128)
+    del w
+    g = torch.Generator(device="cuda").manual_seed(107)
+    x = torch.randn(2048, 4096, device="cuda", generator=g).half()
+    _three(lambda: K.gemm(p, s, x, group=128))
 
 
 CASES = {n[len("case_"):]: f for n, f in globals().items() if n.startswith("case_")}
