@@ -431,6 +431,8 @@ def run_ours(args, rank, world, dev):
         extras["speedup_vs_cublas_per_row"] = round(cublas_us / row_us, 3)
         extras["speedup_vs_cublas_g128_unchained"] = round(cublas_us / g128_plain_us, 3)
         del prow
+        if not args.no_prefill:
+            extras["prefill_gemm"] = prefill_gemm_times(K, dev)
         torch.cuda.empty_cache()
 
 
@@ -640,6 +642,60 @@ def llama8b_times(K, rank, world, dev, stream, peak, reps=200):
     return out
 
 
+def load_tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    return 1590.0, "fallback 1.59 PFLOP/s"
+
+
+def prefill_gemm_times(K, dev, reps=20):
+    """The tensor-core W4A16 GEMM (w4a16_gemm) on Llama-3-8B-shaped layers at prefill
+    batches of 128, 512 and 2048 activation rows, group-128 scales, seeded random weights,
+    against cuBLAS fp16 F.linear on the dense weights and against dequantise-then-cuBLAS
+    (what a layer without a dense copy would run otherwise).  Compute-bound: the int4
+    weights (4-15 MB) stay in L2 across repetitions, which is how a prefill uses them."""
+    import torch.nn.functional as F
+    peak, src = load_tensor_peak()
+    out = {"peak_tflops": peak, "peak_source": src}
+
+    def t(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) * 1000.0 / reps
+
+    for name, (n, k) in (("q_proj", (4096, 4096)), ("gate_up", (14336, 4096)), ("down_proj", (4096, 14336))):
+        g = torch.Generator(device=dev).manual_seed(300 + n + k)
+        w = (torch.randn(n, k, device=dev, generator=g) * 0.02).half()
+        p, s = K.quantize_pack(w, group=GROUP)
+        r = {"rows": n, "cols": k}
+        for m in (128, 512, 2048):
+            x = torch.randn(m, k, device=dev, generator=g).half()
+            if m == 128:  # the same weight the fallback multiplies by, fp32 sums
+                ref = x.float() @ K.dequant_int4(p, s, group=GROUP).float().t()
+                err = (K.gemm(p, s, x, group=GROUP) - ref).abs().max().item()
+                r["max_abs_err_vs_dequantised"] = err
+                r["within_tolerance"] = bool(err <= 1e-3 + 1e-3 * ref.abs().max().item())
+            us = t(lambda: K.gemm(p, s, x, group=GROUP))
+            cu = t(lambda: F.linear(x, w))
+            dq = t(lambda: F.linear(x, K.dequant_int4(p, s, group=GROUP)))
+            tf = 2.0 * m * n * k / us / 1e6
+            r[f"m{m}"] = {"gemm_us": round(us, 2), "tflops": round(tf, 1), "frac_of_peak": round(tf / peak, 4),
+                          "cublas_fp16_us": round(cu, 2), "dequant_cublas_us": round(dq, 2)}
+        out[name] = r
+        del w, p, s
+    torch.cuda.empty_cache()
+    return out
+
+
 def decode_step_times(dev, stream, reps=200):
     """Decode step of the random-init Llama-3.2-1B architecture (16 layers, hidden 2048,
     GQA 32/8, SwiGLU 8192, vocab 128256, tied head), batch 1, KV length 512, replayed
@@ -772,6 +828,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step measurement")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the tensor-core GEMM on prefill batches (128/512/2048 rows)")
     ap.add_argument("--no-llama8b", action="store_true",
                     help="skip the Llama-3-8B-shaped layers (batch 1/4/16, row-sharded over N GPUs)")
     args = ap.parse_args()

@@ -5,7 +5,7 @@
 // w16 is the reference's dequantised weight exactly (`dequant_int4`, the fp16 weight a
 // caller without the dense copy multiplies by; the reference itself runs every call with
 // more than one activation row through F.linear on fp16 weights, src/w4a16/kernels.py:
-// 120-121).  The int4 codes are decoded into shared memory, never into HBM: HBM carries
+// 120-121).  The int4 codes are decoded into tensor memory, never into HBM: HBM carries
 // N*K/2 packed bytes + scales + M*K*2 activation bytes + the output, against 2*N*K more
 // written and read again by dequantise-then-GEMM.
 //
@@ -13,18 +13,22 @@
 //   warp 0       TMA copies per 64-column stage: the activation tile (BN x 64 fp16, 128-byte
 //                swizzle: the tensor core's K-major canonical layout) and the packed weight
 //                tile (128 rows x 32 bytes);
-//   warp 1       allocates BN TMEM columns; one lane issues 4 tcgen05.mma (M=128, N=BN, K=16,
-//                fp16 x fp16 -> fp32 in TMEM) per stage and commits each stage's completion to
-//                the stage's "empty" barrier, the last one to the accumulator barrier;
-//   warps 2..    G decoder groups of four warps (G = 4 for BN = 256, 3 for 128); group g
-//                decodes stages g, g+G, g+2G, ..., so G stages are decoded at once (one warp's pass over a stage is latency-
-//                bound: barrier test, decode, proxy fence, arrive).  Thread r of a group owns
-//                weight row r: it reads the row's 8 packed words of the stage, forms w16 (exact
-//                codes, one fp32 multiply, one rounding to fp16 as the reference's
-//                dequantisation does) and writes the 16-byte chunks into the swizzled K-major A
-//                tile; scales are fetched one stage of the group ahead.  Then the epilogue: the
-//                thread holds TMEM lane r (its warp's lane quarter), reads its group's quarter of
-//                the row's BN accumulators with tcgen05.ld, adds the bias and stores y[m, n] (32
+//   warp 1       allocates the 512 TMEM columns (the fp32 accumulator, then one decoded weight
+//                tile per stage); one lane issues 4 tcgen05.mma per stage (M=128, N=BN, K=16,
+//                A = decoded weights from TMEM, B = activations from shared memory, fp32 sums
+//                in TMEM) and commits each stage's completion to the stage's "empty" barrier,
+//                the last one to the accumulator barrier;
+//   warps 2..    G decoder groups of four warps (G = 3 for BN = 256, 4 for 128); group g decodes
+//                stages g, g+G, g+2G, ..., so G stages are decoded at once (one warp's pass over
+//                a stage is latency-bound: barrier test, decode, TMEM store, arrive).  Thread r of
+//                a group owns weight row r: it reads the row's 8 packed words of the stage, forms
+//                w16 (exact codes, one fp32 multiply, one rounding to fp16 as the reference's
+//                dequantisation does) and stores the row's 64 weights into its own TMEM lane
+//                (tcgen05.st: the weight tile never touches shared memory, whose bandwidth the
+//                activation copies and MMA reads already use); scales are fetched one stage of
+//                the group ahead.  Then the epilogue: the thread holds TMEM lane r (its warp's
+//                lane quarter), reads its group's share of the row's BN accumulators (16-column
+//                chunks dealt round-robin) with tcgen05.ld, adds the bias and stores y[m, n] (32
 //                consecutive n per warp store).
 // BN is 256 when that still gives every SM a tile, else 128.
 // Every barrier wait is bounded (2 s of %globaltimer); a wait that gives up records error 5
@@ -47,13 +51,13 @@ namespace {
 constexpr int kGmRows = 128;     // weight rows per tile: the MMA's M, TMEM lanes
 constexpr int kGmK = 64;         // columns per stage: one 128-byte swizzle atom of fp16
 template <int BN>
-constexpr int gm_stages() { return BN == 128 ? 6 : 4; }  // as deep as 227 KB of shared memory allows
+constexpr int gm_stages() { return BN == 128 ? 8 : 6; }  // as deep as shared memory and TMEM allow
 // Decoder groups (stages decoded at once; a group is one warp per TMEM lane quarter).  The
 // stage count is a multiple of the group count, so every ring slot is always decoded by the
 // same group, in order: a group never waits on a slot's next phase before it has seen the
 // current one complete (a parity wait that ran a phase ahead would pass on the one before).
 template <int BN>
-constexpr int gm_groups() { return BN == 128 ? 3 : 4; }
+constexpr int gm_groups() { return BN == 128 ? 4 : 3; }
 template <int BN>
 constexpr int gm_warps() { return 2 + 4 * gm_groups<BN>(); }  // 0: copies, 1: TMEM + MMA, rest: decode + epilogue
 constexpr int kGmErrWait = 5;    // a pipeline wait gave up
@@ -67,12 +71,16 @@ template <int BN>
 struct GmLayout {
   static constexpr int kStages = gm_stages<BN>();
   static_assert(kStages % gm_groups<BN>() == 0, "each ring slot belongs to one decoder group");
-  static constexpr uint32_t kA = kGmRows * kGmK * 2;  // decoded weights, fp16
   static constexpr uint32_t kB = BN * kGmK * 2;       // activations, fp16
   static constexpr uint32_t kP = kGmRows * kGmK / 2;  // packed weights
-  static constexpr uint32_t kStage = kA + kB + kP;
-  static_assert(kA % 1024 == 0 && kB % 1024 == 0, "swizzled tiles start on 1024-byte boundaries");
+  static constexpr uint32_t kStage = kB + kP;
+  static_assert(kB % 1024 == 0, "swizzled tiles start on 1024-byte boundaries");
   static_assert(kStage % 1024 == 0, "stages start on 1024-byte boundaries");
+  // TMEM columns: the fp32 accumulator [0, BN), then per stage the decoded weight tile
+  // (128 lanes = rows, 64 fp16 = 32 columns of two each)
+  static constexpr uint32_t kTmemA = BN;
+  static constexpr uint32_t kTmemCols = 512;
+  static_assert(kTmemA + kStages * (kGmK / 2) <= kTmemCols, "accumulator and weight stages fit TMEM");
   // [1024 alignment slack][stages][full, decoded, empty barriers per stage, accumulator
   // barrier, TMEM address]
   static constexpr uint32_t kBarOff = kStages * kStage;
@@ -95,14 +103,30 @@ __device__ __forceinline__ uint32_t gm_idesc() {
   return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kGmRows >> 4) << 24);
 }
 
-__device__ __forceinline__ void gm_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
-                                       uint32_t accumulate) {
+// D (+)= A * B^T with A in tensor memory (K-major: lane = row, two fp16 per 32-bit column) and B
+// in shared memory (gm_desc).
+__device__ __forceinline__ void gm_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane, written and waited for.
+__device__ __forceinline__ void gm_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, "
+      "%31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+      "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void gm_commit(uint32_t bar) {
@@ -157,9 +181,9 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
   auto empty_bar = [&](int s) { return bars + (uint32_t)(2 * L::kStages + s) * 8u; };
   const uint32_t acc_bar = bars + 3u * L::kStages * 8u;
   const uint32_t tmem_slot = acc_bar + 8u;
-  auto stage_a = [&](int s) { return base + (uint32_t)s * L::kStage; };
-  auto stage_b = [&](int s) { return stage_a(s) + L::kA; };
+  auto stage_b = [&](int s) { return base + (uint32_t)s * L::kStage; };
   auto stage_p = [&](int s) { return stage_b(s) + L::kB; };
+  auto tmem_a = [&](uint32_t tmem, int s) { return tmem + L::kTmemA + (uint32_t)s * (kGmK / 2); };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -178,9 +202,9 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
     tma_prefetch_desc(&xmap);
     tma_prefetch_desc(&pmap);
   }
-  if (warp == 1) {  // the whole warp allocates BN columns, then gives up the right to allocate more
+  if (warp == 1) {  // the whole warp allocates TMEM, then gives up the right to allocate more
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
-                 "r"(BN)
+                 "r"(L::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -212,18 +236,6 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
             : "memory");
         tma_load_2d(stage_p(s), &pmap, kb * (kGmK / 2), n0, full_bar(s), stream_once);
         ++issued;
-        // warm L2 with the tiles of the stage one ring ahead, so that copy is an L2 hit
-        const int kp = kb + L::kStages;
-        if (kp < nk) {
-          asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                           reinterpret_cast<uint64_t>(&xmap)),
-                       "r"(kp * kGmK), "r"(m0)
-                       : "memory");
-          asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                           reinterpret_cast<uint64_t>(&pmap)),
-                       "r"(kp * (kGmK / 2)), "r"(n0)
-                       : "memory");
-        }
       }
       // the copies this thread issued have all landed before the CTA can exit
       for (int kb = issued - L::kStages < 0 ? 0 : issued - L::kStages; kb < issued; ++kb)
@@ -241,10 +253,11 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
           break;
         }
         gm_fence_after();
-        const uint64_t da = gm_desc(stage_a(s)), db = gm_desc(stage_b(s));
+        const uint32_t ta = tmem_a(tmem_d, s);
+        const uint64_t db = gm_desc(stage_b(s));
 #pragma unroll
-        for (int kk = 0; kk < kGmK / 16; ++kk)  // +32 bytes of K per step: +2 in address units
-          gm_mma(tmem_d, da + 2u * kk, db + 2u * kk, idesc, (kb | kk) != 0);
+        for (int kk = 0; kk < kGmK / 16; ++kk)  // K += 16: +8 TMEM columns of A, +32 bytes of B
+          gm_mma_ts(tmem_d, ta + 8u * kk, db + 2u * kk, idesc, (kb | kk) != 0);
         gm_commit(empty_bar(s));
       }
       gm_commit(acc_bar);  // every MMA issued above (or none) is complete when this arrives
@@ -285,25 +298,22 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
       const uint4 w0 = lds128(stage_p(s) + (uint32_t)r * 32u);
       const uint4 w1 = lds128(stage_p(s) + (uint32_t)r * 32u + 16u);
       const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      const uint32_t arow = stage_a(s) + (uint32_t)r * 128u;
+      uint32_t hv[32];  // row r's 64 weights of the stage, two fp16 per TMEM column
 #pragma unroll
       for (int j = 0; j < 8; ++j) {  // word j: columns 8j..8j+7 of the stage (interleaved packing)
         uint32_t o[4];
         decode_word(words[j], o);  // exact codes, pairs (0,1) (2,3) (4,5) (6,7)
-        uint32_t hv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&o[i]));
           // one packed conversion (round to nearest per element, as two separate ones would)
           const __half2 w2 = __floats2half2_rn(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc));
-          hv[i] = *reinterpret_cast<const uint32_t*>(&w2);
+          hv[4 * j + i] = *reinterpret_cast<const uint32_t*>(&w2);
         }
-        const uint32_t dst = arow + (uint32_t)((j ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(hv[0]), "r"(hv[1]),
-                     "r"(hv[2]), "r"(hv[3])
-                     : "memory");
       }
-      fence_proxy_async_smem();  // the tensor core reads these through the async proxy
+      // into this thread's TMEM lane; complete before the stage is announced
+      gm_st32(tmem_a(tmem_d, s) + ((uint32_t)(quarter * 32) << 16), hv);
+      gm_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dec_bar(s));
     }
@@ -335,7 +345,8 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
   __syncthreads();
   if (warp == 1) {
     gm_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d), "r"(BN)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d),
+                 "r"(L::kTmemCols)
                  : "memory");
   }
 }
