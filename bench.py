@@ -355,6 +355,18 @@ def run_ours(args, rank, world, dev):
         tp_choice["gemv_alone_us"] = round(kernel_us, 3)
         tp_choice["overhead_us"] = {k[:-8]: round(tp_choice[k] - kernel_us, 3)
                                     for k in ("fused_step_us", "nccl_step_us")}
+        # where a fused step's time goes, per rank: the last of 50 chained steps, from the
+        # %globaltimer stamps each rank's kernel writes into its own region (every rank runs
+        # the same steps, then the stamps are gathered)
+        for i in range(50):
+            steps_fns[i % len(steps_fns)]()
+        torch.cuda.synchronize()
+        keys = ("start_wait", "to_done", "done_wait", "total")
+        tl = tpa.timeline()
+        mine = torch.tensor([tl[k] for k in keys], dtype=torch.float64, device=dev)
+        every = torch.empty(world, len(keys), dtype=torch.float64, device=dev)
+        torch.distributed.all_gather_into_tensor(every, mine)
+        tp_choice["timeline_us"] = [{k: round(float(v), 2) for k, v in zip(keys, row)} for row in every.tolist()]
         extras["tensor_parallel"] = tp_choice
     if not args.no_llama8b:
         extras["llama8b"] = llama8b_times(K, rank, world, dev, stream, load_peaks()[0])

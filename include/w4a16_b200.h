@@ -182,6 +182,12 @@ size_t w4a16_tp_ipc_handle_bytes(void);
 int w4a16_tp_region_alloc(size_t out_bytes, void** region, void* ipc_handle);
 int w4a16_tp_region_open(const void* ipc_handle, void** region);
 int w4a16_tp_region_close(void* region, int owned);
+/* The last fused step's timeline of a region's owner (a region allocated or opened in this
+ * process; the owner's kernel writes it into its own region's header): four
+ * %globaltimer stamps in ns — [0] this rank's start flags published, [1] every rank's start
+ * flag seen (first warp of the first CTA), [2] this rank's rows stored and fenced (just before
+ * its done flags), [3] every rank's done flag seen.  Synchronises `stream`. */
+int w4a16_tp_region_timeline(const void* region, unsigned long long* stamps, w4a16_stream_t stream);
 
 /* One step, one kernel: this rank's rows [row0, row0 + rows) of y = W x (interleaved
  * packing, one fp16 vector x [cols], out_dtype fp32 or fp16) are written by the GEMV's

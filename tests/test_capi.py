@@ -111,6 +111,15 @@ def _gemm(lib, packed=1 << 12, scale=1 << 16, group=0, x=1 << 20, bias=None, M=2
                           odt, None)
 
 
+def test_tp_region_timeline_host_validation(lib):
+    stamps = (ctypes.c_ulonglong * 4)()
+    assert lib.w4a16_tp_region_timeline(None, stamps, None) == -1
+    assert lib.w4a16_tp_region_timeline(ctypes.c_void_p(1 << 20), None, None) == -1
+    # a pointer no region call returned: refused before any CUDA call
+    assert lib.w4a16_tp_region_timeline(ctypes.c_void_p(1 << 20), stamps, None) == -2
+    assert b"w4a16_tp_region_alloc" in lib.w4a16_last_error_string()
+
+
 def test_gemm_host_validation(lib):
     # every call fails validation before any CUDA API is reached
     assert _gemm(lib, odt=3) == -4

@@ -131,6 +131,9 @@ def _fused_worker(rank, world, port, rows, cols, group, out_dtype, q):
             ok &= bool((err <= tol + tol * np.abs(ref)).all())
         del graph
         ok &= K.read_device_error() == 0
+        # the last step's stamps: every phase non-negative, the step well under a second
+        tl = tp.timeline()
+        ok &= all(v >= 0 for v in tl.values()) and 0 < tl["total"] < 1e6
         q.put((rank, ok, worst))
     finally:
         if tp is not None:

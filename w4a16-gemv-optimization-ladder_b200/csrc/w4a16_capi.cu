@@ -375,6 +375,27 @@ int w4a16_tp_region_close(void* region, int owned) {
   return W4A16_OK;
 }
 
+int w4a16_tp_region_timeline(const void* region, unsigned long long* stamps, w4a16_stream_t stream) {
+  if (!region || !stamps) {
+    set_error("null pointer argument");
+    return W4A16_ERR_NULL;
+  }
+  size_t cap = 0;
+  if (!region_capacity(region, &cap)) {
+    set_error("region %p was not created by w4a16_tp_region_alloc or mapped by w4a16_tp_region_open in this process", region);
+    return W4A16_ERR_SHAPE;
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(stamps, static_cast<const uint8_t*>(region) + w4a16::kTpTimelineOffset,
+                                  4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_error("reading a region's step timeline: %s", cudaGetErrorString(e));
+    return W4A16_ERR_CUDA;
+  }
+  return W4A16_OK;
+}
+
 int w4a16_gemv_allgather(const uint8_t* packed, const void* scale, int scale_dtype, int group,
                          const void* x, int rows, int cols, int out_dtype, long long row0, int rank,
                          int nranks, void* const* regions, void* workspace, size_t workspace_bytes,

@@ -80,6 +80,10 @@ constexpr int kTpStart = 0;                 // u32 [kMaxRanks]
 constexpr int kTpDone = kMaxRanks;          // u32 [kMaxRanks]
 constexpr int kTpEpoch = 2 * kMaxRanks;     // u32
 constexpr int kTpCtaDone = 2 * kMaxRanks + 1;
+// Step timeline in this rank's own header (u64 %globaltimer ns at byte 192): [0] start flags
+// published, [1] every rank's start flag seen (first warp), [2] this rank's rows stored and
+// fenced (done flags about to be published), [3] every rank's done flag seen.
+constexpr int kTpTimeline = 48;  // u32 index: byte 192
 
 constexpr uint64_t kStageWaitLimitNs = 2000000000ull;  // 2 s; a stage normally lands in us
 constexpr uint64_t kDrainWaitLimitNs = 100000000ull;   // 0.1 s per outstanding stage
@@ -295,6 +299,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const unsigned e = *reinterpret_cast<volatile unsigned*>(p.tp_flags[p.tp_rank] + kTpEpoch) + 1u;
     if (blockIdx.x == 0 && threadIdx.x < p.tp_n)
       st_release_sys(p.tp_flags[threadIdx.x] + kTpStart + p.tp_rank, e);
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+      *reinterpret_cast<volatile unsigned long long*>(p.tp_flags[p.tp_rank] + kTpTimeline) = globaltimer_ns();
   }
 
   // kSchedLocal partial sums [unit of the CTA][16 rows] sit after the staged vector;
@@ -474,6 +480,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           }
         }
     }
+    if (lane == 0 && blockIdx.x == 0 && warp == 0)
+      *reinterpret_cast<volatile unsigned long long*>(tp_my + kTpTimeline + 2) = globaltimer_ns();
     tp_peers_ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
     tp_started = true;
   };
@@ -504,6 +512,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           (__threadfence_system(), atomicAdd(tp_my + kTpCtaDone, 1u) == gridDim.x - 1)) {
         tp_my[kTpCtaDone] = 0u;
         __threadfence_system();
+        *reinterpret_cast<volatile unsigned long long*>(tp_my + kTpTimeline + 4) = globaltimer_ns();
         for (int k = 0; k < p.tp_n; ++k) st_release_sys(p.tp_flags[k] + kTpDone + p.tp_rank, tp_e);
         const uint64_t t0 = globaltimer_ns();
         for (int k = 0; k < p.tp_n; ++k)
@@ -513,6 +522,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
               break;
             }
           }
+        *reinterpret_cast<volatile unsigned long long*>(tp_my + kTpTimeline + 6) = globaltimer_ns();
         tp_my[kTpEpoch] = tp_e;
       }
     }

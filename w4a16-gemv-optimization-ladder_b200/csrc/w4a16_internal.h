@@ -104,6 +104,7 @@ cudaError_t launch_maybe_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 // w4a16_tp_region_alloc; the kernels use header bytes [0, 128) for their flags).
 constexpr size_t kTpHeaderBytes = 256;
 constexpr size_t kTpCapacityOffset = 128;
+constexpr size_t kTpTimelineOffset = 192;  // 4 x u64 step stamps, written by the owner's kernel
 
 // Reads (and clears) the device-side error word written by kernels whose bounded
 // waits ran out.  Synchronises `stream`.

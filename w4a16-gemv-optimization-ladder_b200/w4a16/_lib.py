@@ -53,6 +53,7 @@ SIGNATURES = {
     "w4a16_gemv_allgather": ([_p, _p, _i, _i, _p, _i, _i, _i, ctypes.c_longlong, _i, _i,
                               ctypes.POINTER(ctypes.c_void_p), _p, _sz, _u, _p], _i),
     "w4a16_tp_set_peer_wait_ns": ([ctypes.c_ulonglong], _i),
+    "w4a16_tp_region_timeline": ([_p, _p, _p], _i),
     "w4a16_decode_plan_create": ([_p, ctypes.POINTER(ctypes.c_void_p)], _i),
     "w4a16_decode_plan_destroy": ([_p], _i),
     "w4a16_decode_step": ([_p, _p, _p, _p, _p, _p, _p], _i),

@@ -205,6 +205,24 @@ class FusedAllGatherW4A16:
                     w.zero_()
         return code.value
 
+    def timeline(self, stream=None):
+        """The last step on this rank, from the %globaltimer stamps its kernel wrote into this
+        rank's region (synchronises the stream), in µs: `start_wait` from publishing this
+        rank's start flags until the first warp of the first CTA, about to store its first
+        tile, has seen every rank's start flag (so at least that tile's compute); `to_done`
+        from there until every CTA's rows are stored and fenced; `done_wait` until every
+        rank's done flag is seen; `total` the sum."""
+        from . import kernels as K
+
+        s = stream if stream is not None else K._stream(self.device)
+        t = (ctypes.c_ulonglong * 4)()
+        with torch.cuda.device(self.device):
+            self._check(self.lib.w4a16_tp_region_timeline(ctypes.c_void_p(self.regions[self.rank]), t, s),
+                        "w4a16_tp_region_timeline")
+        t0, t1, t2, t3 = (int(v) for v in t)
+        return {"start_wait": (t1 - t0) / 1e3, "to_done": (t2 - t1) / 1e3, "done_wait": (t3 - t2) / 1e3,
+                "total": (t3 - t0) / 1e3}
+
     def __call__(self, x, pdl=False, check=False):
         if not (isinstance(x, torch.Tensor) and x.dtype == torch.float16 and x.dim() == 1
                 and x.is_contiguous() and x.shape[0] == self.packed.shape[1] * 2 and x.device == self.device):
