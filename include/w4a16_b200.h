@@ -340,10 +340,16 @@ int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int grou
  * keeps no dense copy.  packed uint8 [N][K/2], interleaved packing only, 16-byte aligned;
  * scale fp32 [N] (group 0) or [N][K/128] (group 128); x fp16 [M][K], 16-byte aligned; bias fp32
  * [N] or NULL; y fp32 or fp16 [M][N].  K a multiple of 64 (of 128 with group 128), M, N >= 1,
- * any M and N (ragged tiles are masked).  One CTA per 128 x 128 output tile. */
+ * any M and N (ragged tiles are masked).  One CTA per 128 x 128 or 128 x 256 output tile.
+ * workspace (optional, 256-byte aligned, zero-filled once; NULL or smaller than
+ * w4a16_gemm_workspace_bytes(M, N, K) means no split): when the tiles are fewer than the SMs,
+ * K is split across CTAs and the last CTA of each tile sums the fp32 partial tiles in a fixed
+ * order (results do not depend on which finishes last); the kernel leaves the workspace's
+ * counters zeroed again.  Calls sharing a workspace must be ordered on one stream. */
+size_t w4a16_gemm_workspace_bytes(int M, int N, int K);
 int w4a16_gemm(const uint8_t* packed, const float* scale, int group, const void* x,
-               const float* bias, int M, int N, int K, void* y, int out_dtype,
-               w4a16_stream_t stream);
+               const float* bias, int M, int N, int K, void* y, int out_dtype, void* workspace,
+               size_t workspace_bytes, w4a16_stream_t stream);
 
 /* Reads and clears the error word that kernels set when a bounded wait runs out
  * (0 = none; 1 = a weight copy did not land in time; 2 = another rank's flag did not

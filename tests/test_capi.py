@@ -105,10 +105,10 @@ def test_python_ops_fail_loudly_without_library(monkeypatch, tmp_path):
 
 
 def _gemm(lib, packed=1 << 12, scale=1 << 16, group=0, x=1 << 20, bias=None, M=256, N=256, K=1024,
-          y=1 << 24, odt=0):
+          y=1 << 24, odt=0, ws=None):
     return lib.w4a16_gemm(ctypes.c_void_p(packed), ctypes.c_void_p(scale), group, ctypes.c_void_p(x),
                           None if bias is None else ctypes.c_void_p(bias), M, N, K, ctypes.c_void_p(y),
-                          odt, None)
+                          odt, None if ws is None else ctypes.c_void_p(ws), 1 << 20, None)
 
 
 def test_tp_region_timeline_host_validation(lib):
@@ -134,7 +134,9 @@ def test_gemm_host_validation(lib):
     assert _gemm(lib, x=(1 << 20) + 8) == -3
     assert _gemm(lib, y=(1 << 24) + 2) == -3       # fp32 output 4-byte aligned
     assert _gemm(lib, bias=(1 << 16) + 2) == -3
+    assert _gemm(lib, ws=(1 << 28) + 16) == -3      # workspace 256-byte aligned
     assert b"aligned" in lib.w4a16_last_error_string()
+    assert lib.w4a16_gemm_workspace_bytes(0, 256, 1024) == 0
 
 
 def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0, flags=0):

@@ -28,6 +28,9 @@ CASES = [  # M, N, K, group
     (77, 130, 256, 128),
     (600, 16384, 512, 0),     # 256-row activation tiles (enough tiles for every SM), ragged M
     (1000, 9500, 1024, 128),  # 256-row tiles, ragged M and N
+    (128, 4096, 4096, 128),   # split K: 32 tiles, 4 splits
+    (96, 1000, 1024, 0),      # split K, ragged N, per-row scales
+    (200, 640, 8192, 128),    # split K: 10 tiles, 8 splits
 ]
 
 
@@ -92,3 +95,17 @@ def test_gemm_repeated_calls_and_linear_layer():
     ref = x.reshape(-1, 1024).float() @ w16.t() + layer.bias_f32
     assert ((y1.reshape(-1, 768).float() - ref).abs() <= 2e-3 + 2e-3 * ref.abs()).all()
     assert _device_error() == 0
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 4096, 4096), (200, 640, 8192)], ids=lambda v: str(v))
+def test_gemm_split_k_is_deterministic_and_matches_unsplit(m, n, k):
+    lib = _lib.lib()
+    assert lib.w4a16_gemm_workspace_bytes(m, n, k) > 0  # these shapes split K
+    p, s = _weights(n, k, 128, 11)
+    x = torch.randn(m, k, device="cuda").half()
+    ys = [K.gemm(p, s, x, group=128) for _ in range(3)]  # shared workspace, counters re-armed
+    whole = K.gemm(p, s, x, group=128, workspace=False)
+    torch.cuda.synchronize()
+    assert _device_error() == 0
+    assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])  # fixed summation order
+    assert ((ys[0] - whole).abs() <= 1e-4 * (1.0 + whole.abs())).all()

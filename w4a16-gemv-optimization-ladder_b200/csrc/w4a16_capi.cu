@@ -528,9 +528,11 @@ int w4a16_read_device_error(int* code, w4a16_stream_t stream) {
   return W4A16_OK;
 }
 
+size_t w4a16_gemm_workspace_bytes(int M, int N, int K) { return w4a16::gemm_workspace_bytes(M, N, K); }
+
 int w4a16_gemm(const uint8_t* packed, const float* scale, int group, const void* x,
-               const float* bias, int M, int N, int K, void* y, int out_dtype,
-               w4a16_stream_t stream) {
+               const float* bias, int M, int N, int K, void* y, int out_dtype, void* workspace,
+               size_t workspace_bytes, w4a16_stream_t stream) {
   if (out_dtype != W4A16_DTYPE_F32 && out_dtype != W4A16_DTYPE_F16) {
     set_error("unknown output dtype code %d", out_dtype);
     return W4A16_ERR_DTYPE;
@@ -550,12 +552,12 @@ int w4a16_gemm(const uint8_t* packed, const float* scale, int group, const void*
   }
   const size_t osz = out_dtype == W4A16_DTYPE_F32 ? 4 : 2;
   if (!aligned(packed, 16) || !aligned(x, 16) || !aligned(scale, 4) || !aligned(y, osz) ||
-      (bias && !aligned(bias, 4))) {
-    set_error("misaligned pointer: packed and x need 16 B, scale and bias 4 B, y %zu B", osz);
+      (bias && !aligned(bias, 4)) || (workspace && !aligned(workspace, 256))) {
+    set_error("misaligned pointer: packed and x need 16 B, scale and bias 4 B, y %zu B, workspace 256 B", osz);
     return W4A16_ERR_ALIGN;
   }
-  return w4a16::launch_gemm(packed, scale, group, x, bias, M, N, K, y, out_dtype,
-                            reinterpret_cast<cudaStream_t>(stream));
+  return w4a16::launch_gemm(packed, scale, group, x, bias, M, N, K, y, out_dtype, workspace,
+                            workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int w4a16_decode_plan_create(const w4a16_llama_desc* desc, w4a16_decode_plan* plan) {

@@ -166,6 +166,11 @@ struct GemmParams {
   const float* bias;   // [N] or null
   void* y;             // [M][N] fp32 or fp16
   int M, N, K, group;
+  // split K (gridDim.z splits of kb_per_split stages): per-tile arrival counters and fp32
+  // partial tiles [tile][split][BN columns][128 lanes] in the caller's workspace
+  unsigned* cnt;
+  float* part;
+  int kb_per_split;
 };
 
 template <int BN, typename OT>
@@ -189,7 +194,11 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
   const int lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kGmRows;
   const int m0 = blockIdx.y * BN;
-  const int nk = p.K / kGmK;
+  // this CTA's stages: [kb0, kb0 + nk) of the K / 64 (all of them without a split)
+  const int splits = gridDim.z;
+  const int kb0 = blockIdx.z * p.kb_per_split;
+  const int nk_all = p.K / kGmK;
+  const int nk = (kb0 + p.kb_per_split < nk_all ? p.kb_per_split : nk_all - kb0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < L::kStages; ++s) {
@@ -220,8 +229,8 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
       (void)keep;
       int issued = 0;
       bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % L::kStages, u = kb / L::kStages;
+      for (int i = 0; i < nk; ++i) {  // i: this CTA's stage count, kb: the column block
+        const int kb = kb0 + i, s = i % L::kStages, u = i / L::kStages;
         if (u > 0 && !mbar_wait_bounded(empty_bar(s), (u - 1) & 1, kGmWaitNs)) {
           gm_fail();
           ok = false;
@@ -238,15 +247,15 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
         ++issued;
       }
       // the copies this thread issued have all landed before the CTA can exit
-      for (int kb = issued - L::kStages < 0 ? 0 : issued - L::kStages; kb < issued; ++kb)
-        if (!mbar_wait_bounded(full_bar(kb % L::kStages), (kb / L::kStages) & 1, kGmWaitNs)) gm_fail();
+      for (int i = issued - L::kStages < 0 ? 0 : issued - L::kStages; i < issued; ++i)
+        if (!mbar_wait_bounded(full_bar(i % L::kStages), (i / L::kStages) & 1, kGmWaitNs)) gm_fail();
       (void)ok;
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issue
       const uint32_t idesc = gm_idesc<BN>();
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % L::kStages, u = kb / L::kStages;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % L::kStages, u = i / L::kStages;
         if (!mbar_wait_bounded(full_bar(s), u & 1, kGmWaitNs) ||
             !mbar_wait_bounded(dec_bar(s), u & 1, kGmWaitNs)) {
           gm_fail();
@@ -257,7 +266,7 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
         const uint64_t db = gm_desc(stage_b(s));
 #pragma unroll
         for (int kk = 0; kk < kGmK / 16; ++kk)  // K += 16: +8 TMEM columns of A, +32 bytes of B
-          gm_mma_ts(tmem_d, ta + 8u * kk, db + 2u * kk, idesc, (kb | kk) != 0);
+          gm_mma_ts(tmem_d, ta + 8u * kk, db + 2u * kk, idesc, (i | kk) != 0);
         gm_commit(empty_bar(s));
       }
       gm_commit(acc_bar);  // every MMA issued above (or none) is complete when this arrives
@@ -275,19 +284,19 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
     const int n = n0 + r;
     const bool row_in = n < p.N;
     const int ng = p.group ? p.K / p.group : 1;
-    const int kb_per_group = p.group ? p.group / kGmK : nk;  // stages sharing one scale
-    auto scale_of = [&](int kb) {
-      return (row_in && kb < nk) ? __ldg(p.scale + (size_t)n * ng + kb / kb_per_group) : 0.f;
+    const int kb_per_group = p.group ? p.group / kGmK : nk_all;  // column blocks sharing one scale
+    auto scale_of = [&](int kb) {  // kb: column block of the whole K
+      return row_in ? __ldg(p.scale + (size_t)n * ng + kb / kb_per_group) : 0.f;
     };
     // this group's first stage's scale, and its next stage's already on its way
-    float sc = scale_of(grp);
-    float sc_next = scale_of(grp + kG);
+    float sc = grp < nk ? scale_of(kb0 + grp) : 0.f;
+    float sc_next = grp + kG < nk ? scale_of(kb0 + grp + kG) : 0.f;
     bool ok = true;
-    for (int kb = grp; kb < nk; kb += kG) {
-      const int s = kb % L::kStages, u = kb / L::kStages;
-      if (kb != grp) {
+    for (int i = grp; i < nk; i += kG) {
+      const int s = i % L::kStages, u = i / L::kStages;
+      if (i != grp) {
         sc = sc_next;
-        sc_next = scale_of(kb + kG);
+        sc_next = i + kG < nk ? scale_of(kb0 + i + kG) : 0.f;
       }
       // the decision to stop is warp-uniform: __syncwarp and tcgen05.ld need every lane
       if (!__all_sync(0xffffffffu, mbar_wait_bounded(full_bar(s), u & 1, kGmWaitNs))) {
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
       ok = false;
     }
     gm_fence_after();
-    if (ok) {
+    if (ok && splits == 1) {
       const float b = (p.bias && row_in) ? __ldg(p.bias + n) : 0.f;
       OT* y = static_cast<OT*>(p.y);
       // 16-column chunks of the accumulator dealt round-robin to the groups
@@ -339,10 +348,76 @@ __global__ void __launch_bounds__(gm_warps<BN>() * 32, 1)
           }
         }
       }
+    } else if (ok) {  // split K: this split's partial tile, column by column over the 128 lanes
+      float* part = p.part + ((size_t)(blockIdx.y * gridDim.x + blockIdx.x) * splits + blockIdx.z) *
+                                 (size_t)(BN * kGmRows);
+#pragma unroll 1
+      for (int c0 = grp * 16; c0 < BN; c0 += 16 * kG) {
+        float v[16];
+        gm_ld16(tmem_d + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) __stcg(part + (size_t)(c0 + i) * kGmRows + r, v[i]);
+      }
+      __threadfence();
     }
   }
   gm_fence_before();
   __syncthreads();
+  if (splits > 1) {
+    // The last split to finish a tile sums the partials in split order (the same order
+    // whichever arrives last: deterministic), adds the bias, writes y and re-arms the counter.
+    const uint32_t last_slot = tmem_slot + 4u;
+    unsigned* cnt = p.cnt + (blockIdx.y * gridDim.x + blockIdx.x);
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned prev = atomicAdd(cnt, 1u);
+      asm volatile("st.shared.u32 [%0], %1;" ::"r"(last_slot), "r"((unsigned)(prev == (unsigned)splits - 1u))
+                   : "memory");
+    }
+    __syncthreads();
+    unsigned last;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(last) : "r"(last_slot) : "memory");
+    if (last) {
+      __threadfence();
+      const float* part = p.part + (size_t)(blockIdx.y * gridDim.x + blockIdx.x) * splits * (size_t)(BN * kGmRows);
+      OT* y = static_cast<OT*>(p.y);
+      // float4 pieces (4 lanes of one column), 4 pieces per thread in flight at once
+      constexpr int kVec = BN * kGmRows / 4;
+      const float4* part4 = reinterpret_cast<const float4*>(part);
+      for (int base = threadIdx.x; base < kVec; base += 4 * blockDim.x) {
+        float4 acc[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp = 0; sp < splits; ++sp) {  // split order: the same sum whichever CTA is last
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int e4 = base + u * blockDim.x;
+            if (e4 < kVec) {
+              const float4 v = __ldcg(part4 + (size_t)sp * kVec + e4);
+              acc[u].x += v.x;
+              acc[u].y += v.y;
+              acc[u].z += v.z;
+              acc[u].w += v.w;
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e4 = base + u * blockDim.x;
+          if (e4 >= kVec) continue;
+          const int c = (e4 * 4) / kGmRows, rr = (e4 * 4) % kGmRows, m = m0 + c;
+          if (m >= p.M) continue;
+          const float a4[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int nn = n0 + rr + j;
+            if (nn < p.N) y[(size_t)m * p.N + nn] = from_f32<OT>(a4[j] + (p.bias ? __ldg(p.bias + nn) : 0.f));
+          }
+        }
+      }
+      if (threadIdx.x == 0) *cnt = 0u;
+    }
+  }
   if (warp == 1) {
     gm_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_d),
@@ -418,7 +493,9 @@ int launch_gemm_bn(const uint8_t* packed, const void* x, const GemmParams& prm, 
       return W4A16_ERR_CUDA;
     }
   }
-  const dim3 grid((prm.N + kGmRows - 1) / kGmRows, (prm.M + BN - 1) / BN);
+  const int nk = prm.K / kGmK;
+  const dim3 grid((prm.N + kGmRows - 1) / kGmRows, (prm.M + BN - 1) / BN,
+                  (nk + prm.kb_per_split - 1) / prm.kb_per_split);
   k_gemm_tc<BN, OT><<<grid, gm_warps<BN>() * 32, L::kBytes, stream>>>(xmap, pmap, prm);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -428,10 +505,50 @@ int launch_gemm_bn(const uint8_t* packed, const void* x, const GemmParams& prm, 
   return W4A16_OK;
 }
 
+// How a call is cut up: 256 activation rows per tile when that still gives every SM a tile
+// (half the decode work per flop), else 128; and when even 128-row tiles leave SMs idle, K
+// is split across CTAs (at most 8 splits of at least 8 stages each), the splits' partial
+// tiles summed by the last one to finish.
+struct GemmPlan {
+  bool wide = false;
+  int splits = 1, kb_per_split = 0;
+  size_t workspace = 0;  // bytes: counters (256-byte block) + partial tiles
+};
+
+GemmPlan gemm_plan(int M, int N, int K, int sms) {
+  GemmPlan g;
+  const int nk = K / kGmK, ntn = (N + kGmRows - 1) / kGmRows;
+  const long long tiles256 = (long long)ntn * ((M + 255) / 256);
+  const long long tiles128 = (long long)ntn * ((M + 127) / 128);
+  g.wide = M > 128 && tiles256 >= sms;
+  g.kb_per_split = nk;
+  if (!g.wide && tiles128 < sms) {
+    int s = (int)(sms / tiles128);
+    if (s > 8) s = 8;
+    if (s > nk / 8) s = nk / 8;
+    if (s >= 2) {
+      g.kb_per_split = (nk + s - 1) / s;
+      g.splits = (nk + g.kb_per_split - 1) / g.kb_per_split;
+    }
+  }
+  if (g.splits > 1) {
+    const size_t cnt = ((size_t)tiles128 * 4 + 255) & ~(size_t)255;
+    g.workspace = cnt + (size_t)tiles128 * g.splits * 128 * kGmRows * 4;
+  }
+  return g;
+}
+
 }  // namespace
 
+size_t gemm_workspace_bytes(int M, int N, int K) {
+  int sms = 0;
+  if (M <= 0 || N <= 0 || K < kGmK || current_sm_count(&sms) != W4A16_OK) return 0;
+  return gemm_plan(M, N, K, sms).workspace;
+}
+
 int launch_gemm(const uint8_t* packed, const float* scale, int group, const void* x, const float* bias,
-                int M, int N, int K, void* y, int out_dtype, cudaStream_t stream) {
+                int M, int N, int K, void* y, int out_dtype, void* workspace, size_t workspace_bytes,
+                cudaStream_t stream) {
   GemmParams prm;
   prm.scale = scale;
   prm.bias = bias;
@@ -440,18 +557,27 @@ int launch_gemm(const uint8_t* packed, const float* scale, int group, const void
   prm.N = N;
   prm.K = K;
   prm.group = group;
-  // 256 activation rows per tile halve the decode work per flop; 128 when the wider tiles
-  // would leave SMs idle
+  prm.cnt = nullptr;
+  prm.part = nullptr;
   int sms = 0;
   const int rc = current_sm_count(&sms);
   if (rc != W4A16_OK) return rc;
-  const long long tiles256 = (long long)((N + kGmRows - 1) / kGmRows) * ((M + 255) / 256);
-  const bool wide = M > 128 && tiles256 >= sms;
+  GemmPlan g = gemm_plan(M, N, K, sms);
+  if (g.splits > 1 && (!workspace || workspace_bytes < g.workspace)) {  // no room: no split
+    g.splits = 1;
+    g.kb_per_split = K / kGmK;
+  }
+  prm.kb_per_split = g.kb_per_split;
+  if (g.splits > 1) {
+    const int ntn = (N + kGmRows - 1) / kGmRows, tiles = ntn * ((M + 127) / 128);
+    prm.cnt = static_cast<unsigned*>(workspace);
+    prm.part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (((size_t)tiles * 4 + 255) & ~(size_t)255));
+  }
   if (out_dtype == W4A16_DTYPE_F32)
-    return wide ? launch_gemm_bn<256, float>(packed, x, prm, stream)
-                : launch_gemm_bn<128, float>(packed, x, prm, stream);
-  return wide ? launch_gemm_bn<256, __half>(packed, x, prm, stream)
-              : launch_gemm_bn<128, __half>(packed, x, prm, stream);
+    return g.wide ? launch_gemm_bn<256, float>(packed, x, prm, stream)
+                  : launch_gemm_bn<128, float>(packed, x, prm, stream);
+  return g.wide ? launch_gemm_bn<256, __half>(packed, x, prm, stream)
+                : launch_gemm_bn<128, __half>(packed, x, prm, stream);
 }
 
 int read_gemm_error(int* code, cudaStream_t stream) {

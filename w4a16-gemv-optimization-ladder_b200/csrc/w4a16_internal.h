@@ -120,7 +120,9 @@ int decode_step_launch(DecodePlan* plan, const long long* token, const long long
 int read_decode_step_error(int* code, cudaStream_t stream);
 // Tensor-core W4A16 GEMM for many activation rows (csrc/w4a16_gemm.cu); arguments checked by the caller.
 int launch_gemm(const uint8_t* packed, const float* scale, int group, const void* x, const float* bias,
-                int M, int N, int K, void* y, int out_dtype, cudaStream_t stream);
+                int M, int N, int K, void* y, int out_dtype, void* workspace, size_t workspace_bytes,
+                cudaStream_t stream);
+size_t gemm_workspace_bytes(int M, int N, int K);
 int read_gemm_error(int* code, cudaStream_t stream);
 int decode_plan_timeline(DecodePlan* plan, int enable, unsigned long long* host, size_t capacity,
                          size_t* count, cudaStream_t stream);

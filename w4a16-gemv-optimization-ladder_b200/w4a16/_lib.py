@@ -61,7 +61,8 @@ SIGNATURES = {
     "w4a16_gemv_noalloc": ([_p, _p, _i, _i, _p, _i, _i, _p, _p], _i),
     "w4a16_dequant": ([_p, _i, _p, _i, _i, _i, _i, _p, _p], _i),
     "w4a16_quantize_pack": ([_p, _i, _i, _i, _i, _i, _p, _p, _i, _p], _i),
-    "w4a16_gemm": ([_p, _p, _i, _p, _p, _i, _i, _i, _p, _i, _p], _i),
+    "w4a16_gemm": ([_p, _p, _i, _p, _p, _i, _i, _i, _p, _i, _p, ctypes.c_size_t, _p], _i),
+    "w4a16_gemm_workspace_bytes": ([_i, _i, _i], ctypes.c_size_t),
     "w4a16_read_device_error": ([ctypes.POINTER(ctypes.c_int), _p], _i),
     "w4a16_status_string": ([_i], ctypes.c_char_p),
     "w4a16_last_error_string": ([], ctypes.c_char_p),

@@ -376,12 +376,32 @@ def dequant_int4(packed, scale, group=0, packing="interleaved"):
     return out
 
 
-def gemm(packed, scale, x, *, group=0, bias=None, out_dtype=torch.float32, out=None):
+_GEMM_WS = {}
+
+
+def _gemm_workspace(dev, m, n, k):
+    """The per-device split-K workspace for a GEMM of this size (zero-filled when made, grown
+    outside stream capture only), or None when the call does not split K."""
+    need = int(_lib.lib().w4a16_gemm_workspace_bytes(m, n, k))
+    if need == 0:
+        return None
+    ws = _GEMM_WS.get(dev)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            return None  # no allocation during capture: that call runs unsplit
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)
+        _GEMM_WS[dev] = ws
+    return ws
+
+
+def gemm(packed, scale, x, *, group=0, bias=None, out_dtype=torch.float32, out=None, workspace=None):
     """y [M, N] = x [M, K] @ dequant_int4(packed, scale, group).T (+ bias), fp32 sums, on the
     tensor cores (tcgen05, accumulators in tensor memory); the dequantised weight is formed
-    in shared memory only.  For many activation rows (prefill): the GEMV above is the
-    batch 1..64 path.  Interleaved packing, fp32 scales; K a multiple of 64 (128 with
-    group 128).  Raises RuntimeError on bad input and launches nothing."""
+    on chip only.  For many activation rows (prefill): the GEMV above is the batch 1..64
+    path.  Interleaved packing, fp32 scales; K a multiple of 64 (128 with group 128).
+    workspace: a zero-filled uint8 CUDA tensor of at least w4a16_gemm_workspace_bytes, None
+    for this device's shared one (calls on several streams at once need their own), or False
+    for no split of K.  Raises RuntimeError on bad input and launches nothing."""
     _check_packed(packed)
     n, k = packed.shape[0], packed.shape[1] * 2
     dev = packed.device
@@ -407,9 +427,18 @@ def gemm(packed, scale, x, *, group=0, bias=None, out_dtype=torch.float32, out=N
     if m == 0:
         return out
     with torch.cuda.device(dev):
+        if workspace is None:
+            workspace = _gemm_workspace(dev, m, n, k)
+        elif workspace is False:
+            workspace = None
+        else:
+            _need(isinstance(workspace, torch.Tensor) and workspace.device == dev
+                  and workspace.dtype == torch.uint8 and workspace.is_contiguous(),
+                  "workspace must be a contiguous uint8 tensor on the weights' device")
+        wsb = workspace.numel() if workspace is not None else 0
         status = _lib.lib().w4a16_gemm(_ptr(packed), _ptr(scale), group, _ptr(x),
                                        _ptr(bias) if bias is not None else None, m, n, k, _ptr(out),
-                                       _OUT_DTYPES[out_dtype], _stream(dev))
+                                       _OUT_DTYPES[out_dtype], _ptr(workspace), wsb, _stream(dev))
     _lib.check(status, "w4a16_gemm")
     return out
 
