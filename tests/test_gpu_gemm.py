@@ -109,3 +109,26 @@ def test_gemm_split_k_is_deterministic_and_matches_unsplit(m, n, k):
     assert _device_error() == 0
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])  # fixed summation order
     assert ((ys[0] - whole).abs() <= 1e-4 * (1.0 + whole.abs())).all()
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 4096, 4096), (640, 2048, 1024)], ids=lambda v: str(v))
+def test_gemm_in_cuda_graph(m, n, k):
+    # the first call sizes the workspace outside capture; replays re-arm the split counters
+    p, s = _weights(n, k, 128, 21)
+    x = torch.randn(m, k, device="cuda").half()
+    want = K.gemm(p, s, x, group=128).clone()
+    out = torch.empty(m, n, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        K.gemm(p, s, x, group=128, out=out)
+    torch.cuda.current_stream().wait_stream(st)
+    with torch.cuda.graph(g):
+        K.gemm(p, s, x, group=128, out=out)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+    assert _device_error() == 0
