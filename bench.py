@@ -445,6 +445,7 @@ def run_ours(args, rank, world, dev):
         del prow
         if not args.no_prefill:
             extras["prefill_gemm"] = prefill_gemm_times(K, dev)
+        extras["config_shapes"] = config_shape_times(K, dev, stream, peak)
         torch.cuda.empty_cache()
 
 
@@ -649,6 +650,57 @@ def llama8b_times(K, rank, world, dev, stream, peak, reps=200):
         if fused is not None:
             fused.close()
         out[name] = res
+        del copies, pbuf, sbuf
+        torch.cuda.empty_cache()
+    return out
+
+
+CONFIG_SHAPES = [("per-row 8192x2048", 8192, 2048, 0, torch.float32),
+                 ("g128 8192x2048", 8192, 2048, GROUP, torch.float32),
+                 ("per-row lm_head 128256x2048", 128256, 2048, 0, torch.float32),
+                 ("g128 lm_head 128256x2048", 128256, 2048, GROUP, torch.float32),
+                 ("per-row down_proj 2048x8192 (split K)", 2048, 8192, 0, torch.float32),
+                 ("g128 down_proj 2048x8192 (split K)", 2048, 8192, GROUP, torch.float32),
+                 ("g128 262144x2048, fp16 scales", 262144, 2048, GROUP, torch.float16)]
+
+
+def config_shape_times(K, dev, stream, peak, reps=400):
+    """The smaller single-GPU configurations at batch 1, each timed through the public
+    K.gemv (work-balancing workspace, no chaining) in a CUDA graph that cycles through enough
+    weight copies (random codes, positive scales) to exceed 2x the L2, so no launch finds its
+    weights in L2: µs, algorithmic GB/s (packed bytes + scale bytes) and the fraction of the
+    measured copy peak."""
+    out = {}
+    for name, rows, cols, group, sdt in CONFIG_SHAPES:
+        ssize = 4 if sdt == torch.float32 else 2
+        nsc = rows * (cols // group if group else 1)
+        pbytes, sbytes = rows * cols // 2, nsc * ssize
+        ncopy = max(2, -(-ROTATE_BYTES // (pbytes + sbytes)))
+        g = torch.Generator(device=dev).manual_seed(500 + rows + cols + group)
+        pbuf = torch.randint(0, 256, (ncopy * pbytes,), dtype=torch.uint8, device=dev, generator=g)
+        sbuf = (torch.rand(ncopy * nsc, device=dev, generator=g) * 2e-3 + 2e-3).to(sdt)
+        shape = (rows, cols // group) if group else (rows,)
+        copies = [(pbuf[c * pbytes:(c + 1) * pbytes].view(rows, cols // 2),
+                   sbuf[c * nsc:(c + 1) * nsc].view(*shape)) for c in range(ncopy)]
+        x = torch.randn(cols, device=dev, generator=g).half()
+        y = torch.empty(rows, dtype=torch.float32, device=dev)
+
+        def gemv(c):
+            K.gemv(copies[c][0], copies[c][1], x, group=group, out=y)
+
+        for c in range(2):
+            gemv(c)
+        torch.cuda.synchronize()
+        graph = capture_steps([lambda c=c: gemv(c) for c in range(ncopy)])
+        replays = max(1, reps // ncopy)
+        graph.replay()
+        torch.cuda.synchronize()
+        ms = time_graphs([graph, None], [1, 0], replays, stream)
+        del graph
+        us = ms * 1000.0 / (replays * ncopy)
+        gbs = (pbytes + sbytes) / (us * 1e-6) / 1e9
+        out[name] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+                     "algorithmic_bytes": pbytes + sbytes, "weight_copies": ncopy}
         del copies, pbuf, sbuf
         torch.cuda.empty_cache()
     return out
