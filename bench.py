@@ -659,6 +659,7 @@ CONFIG_SHAPES = [("per-row 8192x2048", 8192, 2048, 0, torch.float32),
                  ("g128 8192x2048", 8192, 2048, GROUP, torch.float32),
                  ("per-row lm_head 128256x2048", 128256, 2048, 0, torch.float32),
                  ("g128 lm_head 128256x2048", 128256, 2048, GROUP, torch.float32),
+                 ("g128 lm_head 128256x2048, fp16 scales", 128256, 2048, GROUP, torch.float16),
                  ("per-row down_proj 2048x8192 (split K)", 2048, 8192, 0, torch.float32),
                  ("g128 down_proj 2048x8192 (split K)", 2048, 8192, GROUP, torch.float32),
                  ("g128 262144x2048, fp16 scales", 262144, 2048, GROUP, torch.float16)]

@@ -15,6 +15,8 @@ times and synchronises; the first launch is the warm-up, so a capture takes
     batch16         lm_head-sized 128256 x 2048 group-128, 16 vectors     (k_gemv_tma, NB 16, 6 warps)
     longk           down-projection-sized 8192 x 14336 group-128, 1 vector (k_gemv_tma, 9 warps)
     gemm            prefill: 2048 activation rows x 4096 x 4096, group-128 (k_gemm_tc)
+    g128_f32        one vector, 65536 x 2048 group-128, fp32 scales    (k_gemv_tma)
+    g128_f16        the same with fp16 scales                           (k_gemv_tma)
 """
 import sys
 
@@ -91,6 +93,21 @@ def case_gemm():
     g = torch.Generator(device="cuda").manual_seed(107)
     x = torch.randn(2048, 4096, device="cuda", generator=g).half()
     _three(lambda: K.gemm(p, s, x, group=128))
+
+
+def _g128(scale_dtype, seed):
+    w, x = _weights(ROWS, COLS, seed)
+    p, s = K.quantize_pack(w, group=128, scale_dtype=scale_dtype)
+    del w
+    _three(lambda: K.gemv(p, s, x, group=128))
+
+
+def case_g128_f32():
+    _g128(torch.float32, 8)
+
+
+def case_g128_f16():
+    _g128(torch.float16, 8)
 
 
 CASES = {n[len("case_"):]: f for n, f in globals().items() if n.startswith("case_")}
