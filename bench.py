@@ -370,7 +370,11 @@ def run_ours(args, rank, world, dev):
         extras["tensor_parallel"] = tp_choice
     if not args.no_llama8b:
         extras["llama8b"] = llama8b_times(K, rank, world, dev, stream, load_peaks()[0])
-    if rank == 0:
+    if rank == 0 and world == 1:
+        # The single-GPU extras (per-row, decode step, ladder, cuBLAS, prefill GEMM, smaller
+        # shapes) run at N = 1 only: at N > 1 the other ranks would go on to the fused steps
+        # of the end-to-end and check sections and wait for rank 0 longer than the peer-wait
+        # limit allows.
         # per-row variant of the same shape
         prow = [make_weights(ROWS, COLS, 0, seed=50 + c, device=dev) for c in range(2)]
         n = min(args.steps, 2000)
