@@ -345,7 +345,8 @@ int w4a16_quantize_pack(const void* w, int w_dtype, int rows, int cols, int grou
  * w4a16_gemm_workspace_bytes(M, N, K) means no split): when the tiles are fewer than the SMs,
  * K is split across CTAs and the last CTA of each tile sums the fp32 partial tiles in a fixed
  * order (results do not depend on which finishes last); the kernel leaves the workspace's
- * counters zeroed again.  Calls sharing a workspace must be ordered on one stream. */
+ * counters zeroed again, except after w4a16_read_device_error reports a non-zero code: then
+ * zero-fill it again.  Calls sharing a workspace must be ordered on one stream. */
 size_t w4a16_gemm_workspace_bytes(int M, int N, int K);
 int w4a16_gemm(const uint8_t* packed, const float* scale, int group, const void* x,
                const float* bias, int M, int N, int K, void* y, int out_dtype, void* workspace,

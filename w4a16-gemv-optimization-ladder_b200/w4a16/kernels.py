@@ -463,10 +463,18 @@ def quantize_pack(w, group=0, packing="interleaved", scale_dtype=torch.float32):
 
 
 def read_device_error(device=None):
-    """Read and clear the device error word (non-zero if a kernel gave up on a wait)."""
+    """Read and clear the device error word (non-zero if a kernel gave up on a wait).
+
+    A kernel that gave up may have left split-K counters set, so after a non-zero code the
+    workspaces this module owns on the device (the GEMV's and the GEMM's) are zero-filled
+    again; workspaces a caller passed in must be zero-filled by the caller."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     code = ctypes.c_int(0)
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().w4a16_read_device_error(ctypes.byref(code), _stream(dev)),
                    "w4a16_read_device_error")
+        if code.value:
+            for buf in (_WORKSPACE.get(dev.index), _GEMM_WS.get(dev)):
+                if buf is not None:
+                    buf.zero_()
     return code.value
