@@ -51,6 +51,9 @@
 #ifndef W4A16_TMA_WARPS
 #define W4A16_TMA_WARPS 12
 #endif
+#ifndef W4A16_DECODE_WARPS  // warps of the decode-step geometry (two CTAs per SM)
+#define W4A16_DECODE_WARPS 8
+#endif
 #ifndef W4A16_TMA_STAGES
 #define W4A16_TMA_STAGES 2
 #endif
@@ -113,6 +116,7 @@ struct TmaParams {
   int ntiles, kslabs, nwin;
   int nwarps;              // warps that receive work
   int sched;               // kSchedStreamK, kSchedStatic or kSchedDynamic
+  int slots;               // kSchedLocal: ring slots the CTA lays out (its largest unit range)
   const void* pro_src;     // prologue source (XM 2: fp32 h [K]; XM 3: fp16 gate|up [2K])
   const float* pro_gamma;  // XM 2: fp32 gamma [K]
   float pro_eps;           // XM 2: epsilon
@@ -157,6 +161,15 @@ struct LocalPlan {
   static constexpr int kBytes = kUnits * ROWS * 4;
 };
 
+// Offset of the staged activation after `slots` ring slots of weights, scales and
+// mbarriers (WARPS * STAGES slots give SmemPlan::kXOff).  A kSchedLocal launch lays out
+// only the units its CTA range holds, so that a following kernel's CTA fits on the same
+// SM while this one runs.
+template <typename L>
+__host__ __device__ constexpr int ring_x_offset(int slots) {
+  return (slots * (L::kWStride + L::kSStride + 8) + 127) / 128 * 128;
+}
+
 // Warp owning unit u of a range split [floor(w*U/T), floor((w+1)*U/T)).
 __device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
   return (int)(((u + 1) * (long long)T - 1) / U);
@@ -164,7 +177,7 @@ __device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
 
 template <int PACK, int GS, typename ST, int NB, typename OT, int WARPS, int STAGES, int SLABS, int RT,
           int XM, bool TP = false>
-__global__ void __launch_bounds__(WARPS * 32, 1)
+__global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS ? 2 : 1)
     k_gemv_tma(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const TmaParams p) {
   using L = StageLayout<SLABS, RT, GS, ST>;
@@ -187,18 +200,21 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   constexpr bool FOLD = W4A16_FOLD && NB == 1;
   constexpr bool FOLDLO = FOLD && GS && W4A16_FOLD_LO;
   constexpr bool ROWFOLD = FOLD && !GS && W4A16_ROW_NORESET;
-  using Plan = SmemPlan<WARPS, STAGES, L>;
+  static_assert(ring_x_offset<L>(WARPS * STAGES) == SmemPlan<WARPS, STAGES, L>::kXOff, "ring layout");
   // after the rings: [staged x: 2K bytes if XS][128-byte scratch][FOLD corrections:
   // K/128 group floats, then (ROWFOLD) nwin window sums, 128-byte padded][kSchedLocal
   // partial sums]
-  const uint32_t xs = base + (uint32_t)Plan::kXOff;
+  // only one-vector launches take kSchedLocal (batched ones keep the compile-time layout)
+  const bool local = NB == 1 && p.sched == kSchedLocal;
+  // ring slots laid out: the CTA range's units under kSchedLocal, else STAGES per warp
+  const int nslots = local ? p.slots : WARPS * STAGES;
+  const uint32_t xs = base + (uint32_t)ring_x_offset<L>(nslots);
   const uint32_t red_off = XS ? (uint32_t)p.K * 2u : 0u;
   const uint32_t corr = xs + red_off + 128u;
   const uint32_t corr_bytes =
       FOLD ? (uint32_t)((((p.K >> 7) + (ROWFOLD ? p.nwin : 0)) * 4 + 127) & ~127) : 0u;
   const uint32_t corrw = corr + (uint32_t)(p.K >> 7) * 4u;  // ROWFOLD window sums
 
-  const bool local = p.sched == kSchedLocal;
   const int ks = p.kslabs;
   const int nwin = p.nwin;
   // kSchedLocal: this CTA's tiles [tb0, tb0 + ntl) and their units, split over its warps
@@ -233,12 +249,18 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int first_win = (int)(u0 - (long long)first_tile * nwin);
   const int count = active ? (int)(u1 - u0) : 0;
 
-  const uint32_t wring = base + (uint32_t)(warp * STAGES * L::kWStride);
-  const uint32_t sring = base + (uint32_t)(Plan::kScaleOff + warp * STAGES * L::kSStride);
-  const uint32_t bar0 = base + (uint32_t)(Plan::kBarOff + warp * STAGES * 8);
+  // [W slots: nslots x kWStride][scale slots: nslots x kSStride][mbarriers: nslots x 8].
+  // A warp's ring is STAGES consecutive slots from slot0; under kSchedLocal its units
+  // (count <= STAGES, no wrap) take the slots of their places in the CTA range.
+  // (gw * U / T is u0 - tb0 * nwin under kSchedLocal; it does not wait for a tile claim)
+  const int slot0 = local ? (int)((long long)gw * U / T) : warp * STAGES;
+  const uint32_t wring = base + (uint32_t)(slot0 * L::kWStride);
+  const uint32_t sring = base + (uint32_t)(nslots * L::kWStride + slot0 * L::kSStride);
+  const uint32_t bar0 = base + (uint32_t)(nslots * (L::kWStride + L::kSStride) + slot0 * 8);
 
   if (lane == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(bar0 + 8 * s, 1);
+    for (int s = 0; s < STAGES; ++s)
+      if (!local || s < count) mbar_init(bar0 + 8 * s, 1);
     mbar_fence_init();
     tma_prefetch_desc(&wmap);
     if (GS) tma_prefetch_desc(&smap);
@@ -283,6 +305,14 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
 
 #pragma unroll 1
   for (int s = 0; s < STAGES; ++s) issue_one();
+
+  // RMSNorm: gamma is a weight, not the previous kernel's output; a thread's first chunk
+  // of it is loaded before the dependency wait below.
+  float4 g0[2] = {};
+  if (XM == kXRmsNorm && (int)threadIdx.x < (p.K >> 3)) {
+    g0[0] = __ldg(reinterpret_cast<const float4*>(p.pro_gamma) + 2 * threadIdx.x);
+    g0[1] = __ldg(reinterpret_cast<const float4*>(p.pro_gamma) + 2 * threadIdx.x + 1);
+  }
 
   // Everything above touches only the weights and this call's workspace.  Under a
   // programmatic dependent launch the previous kernel may still be running: wait for
@@ -387,12 +417,20 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     } else if (XM == kXRmsNorm) {
       const float4* h4 = static_cast<const float4*>(p.pro_src);
       const float4* g4 = reinterpret_cast<const float4*>(p.pro_gamma);
+      // A thread's first chunk of h stays in registers for the second pass (and its first
+      // chunk of gamma is already there), so a vector of at most one chunk per thread
+      // costs one round trip to L2, not two.
+      float4 h0[2] = {};
       float ss = 0.f;
 #pragma unroll
       for (int j = 0; j < kStageChunks; ++j) {
         const int c = threadIdx.x + j * WARPS * 32;
         if (c < nch) {
           const float4 a = __ldcg(h4 + 2 * c), b = __ldcg(h4 + 2 * c + 1);
+          if (j == 0) {
+            h0[0] = a;
+            h0[1] = b;
+          }
           ss = fmaf(a.x, a.x, ss);
           ss = fmaf(a.y, a.y, ss);
           ss = fmaf(a.z, a.z, ss);
@@ -417,8 +455,8 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
         const int c = threadIdx.x + j * WARPS * 32;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (c < nch) {
-          const float4 a = __ldcg(h4 + 2 * c), b = __ldcg(h4 + 2 * c + 1);
-          const float4 ga = __ldg(g4 + 2 * c), gb = __ldg(g4 + 2 * c + 1);
+          const float4 a = j == 0 ? h0[0] : __ldcg(h4 + 2 * c), b = j == 0 ? h0[1] : __ldcg(h4 + 2 * c + 1);
+          const float4 ga = j == 0 ? g0[0] : __ldg(g4 + 2 * c), gb = j == 0 ? g0[1] : __ldg(g4 + 2 * c + 1);
           v.x = pack_half2(a.x * r * ga.x, a.y * r * ga.y);
           v.y = pack_half2(a.z * r * ga.z, a.w * r * ga.w);
           v.z = pack_half2(b.x * r * gb.x, b.y * r * gb.y);
@@ -443,7 +481,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
           for (int i = 0; i < 4; ++i) {
             const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gw4[i]));
             const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uw4[i]));
-            pk[i] = pack_half2(g2.x / (1.0f + expf(-g2.x)) * u2.x, g2.y / (1.0f + expf(-g2.y)) * u2.y);
+            // silu with the fast exponential and division intrinsics (for g -> -inf the
+            // divisor overflows and the quotient is 0, as silu's limit)
+            pk[i] = pack_half2(__fdividef(g2.x, 1.0f + __expf(-g2.x)) * u2.x,
+                               __fdividef(g2.y, 1.0f + __expf(-g2.y)) * u2.y);
           }
           v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = PACK == W4A16_PACK_SIMPLE ? simple_order(v) : v;
@@ -914,10 +955,20 @@ constexpr int kTileRows = kMmaRows * kRT;
 #ifndef W4A16_LONGK_WARPS
 #define W4A16_LONGK_WARPS 9
 #endif
-enum GeometryKind : int { kGeoDefault = 0, kGeoWide = 1, kGeoLong = 2 };
+// DECODE (a staged one-vector launch whose whole matrix fits its CTAs' rings at once, as in
+// a decode step): W4A16_DECODE_WARPS warps capped at 128 registers (two CTAs per SM) with
+// only the ring slots their units need, so that the next chained kernel's CTA is resident
+// beside this one and streams its weights while this one runs.
+static_assert(W4A16_DECODE_WARPS <= 8 && W4A16_DECODE_WARPS != kWarps &&
+                  W4A16_DECODE_WARPS != W4A16_BATCH_WARPS && W4A16_DECODE_WARPS != W4A16_LONGK_WARPS,
+              "the two-CTA register bound goes by warp count");
+enum GeometryKind : int { kGeoDefault = 0, kGeoWide = 1, kGeoLong = 2, kGeoDecode = 3 };
 template <int GEO>
 struct Geometry {
-  static constexpr int kW = GEO == kGeoWide ? W4A16_BATCH_WARPS : GEO == kGeoLong ? W4A16_LONGK_WARPS : kWarps;
+  static constexpr int kW = GEO == kGeoWide     ? W4A16_BATCH_WARPS
+                            : GEO == kGeoLong   ? W4A16_LONGK_WARPS
+                            : GEO == kGeoDecode ? W4A16_DECODE_WARPS
+                                                : kWarps;
   static constexpr int kS = kStages;
   static constexpr int kR = GEO == kGeoWide ? W4A16_BATCH_RT : kRT;
   static constexpr int kTile = kMmaRows * kR;
@@ -1040,7 +1091,12 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   else
     prm.sched = kSchedStreamK;
   prm.nwarps = (int)(prm.sched == kSchedStreamK ? tk : prm.sched == kSchedLocal ? g_local * kWarps : tt);
-  if (prm.sched == kSchedLocal) smem = smem_base + LP::kBytes;
+  prm.slots = kWarps * kStages;
+  if (prm.sched == kSchedLocal) {
+    // every CTA range holds at most tiles_per_cta * nwin units (<= kWarps * kStages)
+    prm.slots = (int)(tiles_per_cta * prm.nwin);
+    smem = ring_x_offset<L>(prm.slots) + 1024 + tail_smem_bytes<PACK, NB, XM>(p.K) + LP::kBytes;
+  }
   prm.pro_src = p.pro_src;
   prm.pro_gamma = p.pro_gamma;
   prm.pro_eps = p.pro_eps;
@@ -1082,6 +1138,16 @@ int launch_generic(const GemvProblem& p, const __half* x, int M, void* y) {
 }
 
 
+// Whether a one-vector launch of geometry GEO takes kSchedLocal (launch_tma's test on tiles).
+template <int GEO>
+bool local_fits(const GemvProblem& p, const DeviceInfo& di) {
+  using G = Geometry<GEO>;
+  const long long ntiles = (p.N + G::kTile - 1) / G::kTile;
+  const long long nwin = (p.K / kSlabCols + kSlabs - 1) / kSlabs;
+  const long long g_local = ntiles < di.sms ? ntiles : di.sms;
+  return p.split_k != 1 && g_local > 0 && (ntiles + g_local - 1) / g_local * nwin <= (long long)G::kW * G::kS;
+}
+
 template <int PACK, int GS, typename ST, typename OT>
 int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma,
              const DeviceInfo& di, int dev) {
@@ -1119,11 +1185,16 @@ int run_pass(const GemvProblem& p, const __half* x, int M, void* y, bool use_tma
       return W4A16_ERR_SHAPE;
     }
     if constexpr (PACK == W4A16_PACK_INTERLEAVED) {
+      const bool dec = local_fits<kGeoDecode>(p, di) &&
+                       p.K <= kStageChunks * 8 * Geometry<kGeoDecode>::kW * 32;
       if (p.prologue == W4A16_PROLOGUE_RMSNORM)
-        return launch_tma<PACK, GS, ST, 1, OT, kXRmsNorm>(p, x, M, y, di, dev);
+        return dec ? launch_tma<PACK, GS, ST, 1, OT, kXRmsNorm, false, kGeoDecode>(p, x, M, y, di, dev)
+                   : launch_tma<PACK, GS, ST, 1, OT, kXRmsNorm>(p, x, M, y, di, dev);
       if (p.prologue == W4A16_PROLOGUE_SWIGLU)
-        return launch_tma<PACK, GS, ST, 1, OT, kXSwiGlu>(p, x, M, y, di, dev);
-      return launch_tma<PACK, GS, ST, 1, OT, kXCopy>(p, x, M, y, di, dev);
+        return dec ? launch_tma<PACK, GS, ST, 1, OT, kXSwiGlu, false, kGeoDecode>(p, x, M, y, di, dev)
+                   : launch_tma<PACK, GS, ST, 1, OT, kXSwiGlu>(p, x, M, y, di, dev);
+      return dec ? launch_tma<PACK, GS, ST, 1, OT, kXCopy, false, kGeoDecode>(p, x, M, y, di, dev)
+                 : launch_tma<PACK, GS, ST, 1, OT, kXCopy>(p, x, M, y, di, dev);
     }
     set_error("the staged (fused) GEMV takes the interleaved packing");
     return W4A16_ERR_DTYPE;
