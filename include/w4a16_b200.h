@@ -58,7 +58,7 @@ enum w4a16_prologue { W4A16_PROLOGUE_NONE = 0, W4A16_PROLOGUE_RMSNORM = 1, W4A16
  * that kernel to finish before reading anything the kernel wrote, and lets the next
  * kernel start in turn.  Use it between these entries (a normal launch before or after
  * is unaffected); two consecutive calls must not share a workspace or scratch buffer. */
-enum w4a16_launch_flags { W4A16_LAUNCH_PDL = 1 };
+enum w4a16_launch_flags { W4A16_LAUNCH_PDL = 1, W4A16_LAUNCH_SWIGLU_OUT = 2 };
 
 /* ---------------------------------------------------------------------------
  * Reference-mirroring entry points: out[r] = sum_k q[r][k] * scale * vec[k], fp32.
@@ -142,7 +142,12 @@ int w4a16_gemv(const uint8_t* packed, int packing, const void* scale, int scale_
  * vector to sit in shared memory beside the weight rings (cols <= 10752 with group-128
  * fp32 scales, <= 16640 with one scale per row).  out (fp32 or fp16 [rows]) may alias
  * bias (fp32): out = W x + bias is then an in-place residual add.  out must not overlap
- * src.  flags: 0 or W4A16_LAUNCH_PDL. */
+ * src.  flags: W4A16_LAUNCH_PDL and, with the RMSNorm prologue only,
+ * W4A16_LAUNCH_SWIGLU_OUT: the rows are gate / up pairs in blocks of 16 (rows 16b..16b+7
+ * the gate rows and 16b+8..16b+15 the up rows of outputs 8b..8b+7), and out holds
+ * rows / 2 values out[8b+i] = silu(y[16b+i]) * y[16b+8+i] of y = W x in fp32, rounded
+ * once to out_dtype (a Llama MLP's gate|up projection with its activation applied in the
+ * epilogue); rows % 16 == 0 and bias == NULL. */
 int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, int group,
                      int prologue, const void* src, const float* gamma, float eps, int rows,
                      int cols, void* out, int out_dtype, const float* bias, void* workspace,

@@ -139,16 +139,22 @@ def test_gemm_host_validation(lib):
     assert lib.w4a16_gemm_workspace_bytes(0, 256, 1024) == 0
 
 
-def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0, flags=0):
+def _fused(lib, prologue=1, src=1 << 16, gamma=1 << 20, rows=16, cols=256, out=1 << 12, odt=0, flags=0,
+           bias=None):
     return lib.w4a16_gemv_fused(ctypes.c_void_p(1 << 12), ctypes.c_void_p(1 << 12), 0, 0, prologue,
                                 ctypes.c_void_p(src), ctypes.c_void_p(gamma), 1e-5, rows, cols,
-                                ctypes.c_void_p(out), odt, None, None, 0, flags, None)
+                                ctypes.c_void_p(out), odt, bias, None, 0, flags, None)
 
 
 def test_fused_gemv_host_validation(lib):
     assert _fused(lib, prologue=3) == -4                 # NONE, RMSNorm or SwiGLU only
     assert _fused(lib, prologue=7) == -4
-    assert _fused(lib, flags=2) == -4                    # only W4A16_LAUNCH_PDL
+    assert _fused(lib, flags=4) == -4                    # W4A16_LAUNCH_PDL | W4A16_LAUNCH_SWIGLU_OUT only
+    # SwiGLU epilogue: RMSNorm prologue, rows in whole 16-row gate / up blocks, no bias
+    assert _fused(lib, prologue=0, flags=2) == -2
+    assert _fused(lib, prologue=2, flags=2) == -2
+    assert _fused(lib, rows=24, flags=2) == -2
+    assert _fused(lib, flags=2, bias=ctypes.c_void_p(1 << 24)) == -2
     assert _fused(lib, prologue=0, out=(1 << 16) + 256) == -2   # x fp16 [256] = 512 bytes
     assert _fused(lib, src=0) == -1
     assert _fused(lib, gamma=0) == -1                    # RMSNorm needs gamma

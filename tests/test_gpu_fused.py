@@ -60,6 +60,29 @@ def test_gemv_rmsnorm_matches_oracle(rows, cols, group, out_dtype):
     _close(y.float().cpu().numpy(), ref, rel=2e-3 if out_dtype == torch.float32 else 4e-3)
 
 
+@pytest.mark.parametrize("rows,cols,group", [(16384, 2048, 128), (3072, 2048, 128), (512, 256, 0),
+                                             (57344, 4096, 128)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_gemv_rmsnorm_swiglu_out_matches_oracle(rows, cols, group, out_dtype):
+    """Gate|up projection with the SwiGLU epilogue: rows 16b..16b+7 are gate rows and
+    16b+8..16b+15 their up rows; out[8b+i] = silu(y[16b+i]) * y[16b+8+i] of the oracle
+    GEMV's sums (decode-step gate/up with CTA-local reduction, a small per-row matrix, and
+    Llama-3-8B's 2 x 14336 rows on whole-tile schedules)."""
+    packed, scale, pk, s = _weights(rows, cols, group, seed=5 * rows + cols)
+    torch.manual_seed(9)
+    h = torch.randn(cols, device="cuda") * 3.0
+    gamma = torch.rand(cols, device="cuda") + 0.5
+    y = K.gemv_rmsnorm(packed, scale, h, gamma, 1e-5, group=group, out_dtype=out_dtype, swiglu_out=True)
+    assert y.dtype == out_dtype and y.shape == (rows // 2,)
+    full = _oracle(pk, s, _rmsnorm_np(h.cpu().numpy(), gamma.cpu().numpy(), 1e-5), group).reshape(-1, 2, 8)
+    g, u = full[:, 0].reshape(-1), full[:, 1].reshape(-1)
+    ref = g / (1.0 + np.exp(-g)) * u
+    _close(y.float().cpu().numpy(), ref, rel=2e-3 if out_dtype == torch.float32 else 4e-3)
+    with pytest.raises(RuntimeError):
+        K.gemv_rmsnorm(packed, scale, h, gamma, 1e-5, group=group, bias=torch.zeros(rows, device="cuda"),
+                       swiglu_out=True)
+
+
 @pytest.mark.parametrize("rows,cols,group", [(2048, 8192, 128), (2048, 2048, 0), (512, 10752, 128)])  # 10752: the longest group-128 vector that fits
 def test_gemv_swiglu_matches_oracle(rows, cols, group):
     packed, scale, pk, s = _weights(rows, cols, group, seed=3 * rows + cols)

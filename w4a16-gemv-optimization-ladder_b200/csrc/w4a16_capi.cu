@@ -210,9 +210,15 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
     set_error("unknown prologue code %d", prologue);
     return W4A16_ERR_DTYPE;
   }
-  if (flags & ~(unsigned)W4A16_LAUNCH_PDL) {
+  if (flags & ~(unsigned)(W4A16_LAUNCH_PDL | W4A16_LAUNCH_SWIGLU_OUT)) {
     set_error("unknown launch flags 0x%x", flags);
     return W4A16_ERR_DTYPE;
+  }
+  const bool swiglu_out = (flags & W4A16_LAUNCH_SWIGLU_OUT) != 0;
+  if (swiglu_out && (prologue != W4A16_PROLOGUE_RMSNORM || bias || rows % 16 != 0)) {
+    set_error("W4A16_LAUNCH_SWIGLU_OUT needs the RMSNorm prologue, no bias and rows %% 16 == 0 (got %d)",
+              rows);
+    return W4A16_ERR_SHAPE;
   }
   // src stands in for x in the shared checks (16-byte alignment, non-NULL)
   int rc = check_gemv(packed, W4A16_PACK_INTERLEAVED, scale, scale_dtype, group, src, 1, rows, cols,
@@ -234,7 +240,7 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
     const uintptr_t s0 = reinterpret_cast<uintptr_t>(src);
     const uintptr_t s1 = s0 + (size_t)cols * (prologue == W4A16_PROLOGUE_NONE ? 2 : 4);
     const uintptr_t o0 = reinterpret_cast<uintptr_t>(out);
-    const uintptr_t o1 = o0 + (size_t)rows * (out_dtype == W4A16_DTYPE_F32 ? 4 : 2);
+    const uintptr_t o1 = o0 + (size_t)(swiglu_out ? rows / 2 : rows) * (out_dtype == W4A16_DTYPE_F32 ? 4 : 2);
     if (s0 < o1 && o0 < s1) {
       set_error("out overlaps the prologue source");
       return W4A16_ERR_SHAPE;
@@ -261,6 +267,7 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
   p.pro_eps = eps;
   p.staged = true;
   p.pdl = (flags & W4A16_LAUNCH_PDL) != 0;
+  p.out_swiglu = swiglu_out;
   p.stream = reinterpret_cast<cudaStream_t>(stream);
   return w4a16::launch_gemv(p);
 }

@@ -196,6 +196,10 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// silu(g) * u = g / (1 + exp(-g)) * u with the fast exponential and division intrinsics
+// (for g -> -inf the divisor overflows and the quotient is 0, silu's limit).
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
+
 // Two floats rounded to fp16 (round to nearest even), packed low | high.
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return (uint32_t)__half_as_ushort(__float2half_rn(lo)) |

@@ -117,6 +117,7 @@ struct TmaParams {
   int nwarps;              // warps that receive work
   int sched;               // kSchedStreamK, kSchedStatic or kSchedDynamic
   int slots;               // kSchedLocal: ring slots the CTA lays out (its largest unit range)
+  int out_swiglu;          // rows 16b+i / 16b+8+i are a gate / up pair: y[8b+i] = silu(g) * u
   const void* pro_src;     // prologue source (XM 2: fp32 h [K]; XM 3: fp16 gate|up [2K])
   const float* pro_gamma;  // XM 2: fp32 gamma [K]
   float pro_eps;           // XM 2: epsilon
@@ -177,7 +178,7 @@ __device__ __forceinline__ int warp_of_unit(long long u, long long U, int T) {
 
 template <int PACK, int GS, typename ST, int NB, typename OT, int WARPS, int STAGES, int SLABS, int RT,
           int XM, bool TP = false>
-__global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS ? 2 : 1)
+__global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS && WARPS <= 8 ? 2 : 1)
     k_gemv_tma(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                const TmaParams p) {
   using L = StageLayout<SLABS, RT, GS, ST>;
@@ -206,6 +207,8 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS ? 2 : 
   // partial sums]
   // only one-vector launches take kSchedLocal (batched ones keep the compile-time layout)
   const bool local = NB == 1 && p.sched == kSchedLocal;
+  // SwiGLU epilogue (gate|up projection of a decode step): compiled into the RMSNorm kernels
+  const bool swo = XM == kXRmsNorm && NB == 1 && p.out_swiglu != 0;
   // ring slots laid out: the CTA range's units under kSchedLocal, else STAGES per warp
   const int nslots = local ? p.slots : WARPS * STAGES;
   const uint32_t xs = base + (uint32_t)ring_x_offset<L>(nslots);
@@ -481,10 +484,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS ? 2 : 
           for (int i = 0; i < 4; ++i) {
             const float2 g2 = __half22float2(*reinterpret_cast<const __half2*>(&gw4[i]));
             const float2 u2 = __half22float2(*reinterpret_cast<const __half2*>(&uw4[i]));
-            // silu with the fast exponential and division intrinsics (for g -> -inf the
-            // divisor overflows and the quotient is 0, as silu's limit)
-            pk[i] = pack_half2(__fdividef(g2.x, 1.0f + __expf(-g2.x)) * u2.x,
-                               __fdividef(g2.y, 1.0f + __expf(-g2.y)) * u2.y);
+            pk[i] = pack_half2(silu_mul(g2.x, u2.x), silu_mul(g2.y, u2.y));
           }
           v = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(xsp + xs_offset(c * 8)) = PACK == W4A16_PACK_SIMPLE ? simple_order(v) : v;
@@ -680,6 +680,14 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS ? 2 : 
     }
     // Fragment (rt, h, i): row cur_tile*kRows + rt*16 + g (+8 for i >= 2), batch
     // column n = h*8 + 2t + (i & 1).
+    if (swo && tile_w0 == 0 && tile_done) {  // rows g and g + 8 of each block: a gate / up pair
+#pragma unroll
+      for (int rt = 0; rt < RT; ++rt) {
+        const int r0 = cur_tile * kRows + rt * 16;
+        if (t == 0 && r0 < p.N) store_out(r0 / 2 + g, r0 / 2 + g, silu_mul(tot[rt][0][0], tot[rt][0][2]));
+      }
+      continue;
+    }
     if (tile_w0 == 0 && tile_done) {  // the whole tile was summed here
       tp_ensure_started();
 #pragma unroll
@@ -768,6 +776,25 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS ? 2 : 
     if constexpr (NB == 1) {
       __syncthreads();
       tp_ensure_started();
+      if (swo) {  // gate / up pairs (rows 16b + i, 16b + 8 + i) -> output 8b + i
+        for (int i = threadIdx.x; i < ntl * (kRows / 2); i += blockDim.x) {
+          const int tl = i / (kRows / 2), pr = i - tl * (kRows / 2);
+          const int rl = (pr >> 3) * 16 + (pr & 7);  // gate row in the tile; its up row is rl + 8
+          const long long tu0 = (long long)tl * nwin;
+          if (warp_of_unit(tu0, U, T) == warp_of_unit(tu0 + nwin - 1, U, T)) continue;  // written
+          const int r = (tb0 + tl) * kRows + rl;
+          if (r >= p.N) continue;
+          float vg = 0.f, vu = 0.f;
+          for (int w = 0; w < nwin; ++w) {
+            vg += lpart[(tl * nwin + w) * kRows + rl];
+            vu += lpart[(tl * nwin + w) * kRows + rl + 8];
+          }
+          const int o = (tb0 + tl) * (kRows / 2) + pr;
+          store_out(o, o, silu_mul(vg, vu));
+        }
+        tp_warp_done();
+        return;
+      }
       for (int i = threadIdx.x; i < ntl * kRows; i += blockDim.x) {
         const int tl = i / kRows, rl = i - tl * kRows;
         const long long tu0 = (long long)tl * nwin;
@@ -959,7 +986,7 @@ constexpr int kTileRows = kMmaRows * kRT;
 // a decode step): W4A16_DECODE_WARPS warps capped at 128 registers (two CTAs per SM) with
 // only the ring slots their units need, so that the next chained kernel's CTA is resident
 // beside this one and streams its weights while this one runs.
-static_assert(W4A16_DECODE_WARPS <= 8 && W4A16_DECODE_WARPS != kWarps &&
+static_assert(W4A16_DECODE_WARPS <= 16 && W4A16_DECODE_WARPS != kWarps &&
                   W4A16_DECODE_WARPS != W4A16_BATCH_WARPS && W4A16_DECODE_WARPS != W4A16_LONGK_WARPS,
               "the two-CTA register bound goes by warp count");
 enum GeometryKind : int { kGeoDefault = 0, kGeoWide = 1, kGeoLong = 2, kGeoDecode = 3 };
@@ -1001,12 +1028,9 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   constexpr int kTileRows = G::kTile;
   using L = StageLayout<kSlabs, kRT, GS, ST>;
   auto kernel = k_gemv_tma<PACK, GS, ST, NB, OT, kWarps, kStages, kSlabs, kRT, XM, TP>;
+  // full rings; a kSchedLocal launch lays out only its units (checked below)
   const int smem_base = tma_smem_bytes<GS, ST, GEO>() + tail_smem_bytes<PACK, NB, XM>(p.K);
   int smem = smem_base;
-  if (smem > di.smem_optin) {
-    set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
-    return W4A16_ERR_SHAPE;
-  }
   static std::atomic<uint64_t> configured{0};
   const uint64_t bit = 1ull << dev;
   if (!(configured.load(std::memory_order_acquire) & bit)) {
@@ -1080,13 +1104,16 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   using LP = LocalPlan<kWarps, kStages, kTileRows>;
   const int g_local = prm.ntiles < di.sms ? prm.ntiles : di.sms;
   const long long tiles_per_cta = (prm.ntiles + g_local - 1) / (g_local > 0 ? g_local : 1);
-  const bool local_ok = NB == 1 && M == 1 && p.split_k != 1 && g_local > 0 &&
-                        tiles_per_cta * prm.nwin <= LP::kUnits && smem_base + LP::kBytes <= di.smem_optin;
+  const bool local_fit = g_local > 0 && tiles_per_cta * prm.nwin <= LP::kUnits;
+  const int local_smem = local_fit ? ring_x_offset<L>((int)(tiles_per_cta * prm.nwin)) + 1024 +
+                                         tail_smem_bytes<PACK, NB, XM>(p.K) + LP::kBytes
+                                   : 0;
+  const bool local_ok = NB == 1 && M == 1 && p.split_k != 1 && local_fit && local_smem <= di.smem_optin;
   if (local_ok)
     prm.sched = kSchedLocal;
   else if (!have_ws)
     prm.sched = kSchedStatic;
-  else if (prm.ntiles * 4 >= slots || prm.nwin <= 2)
+  else if (prm.ntiles * 4 >= slots || prm.nwin <= 2 || p.out_swiglu)  // whole tiles per warp
     prm.sched = kSchedDynamic;
   else
     prm.sched = kSchedStreamK;
@@ -1095,8 +1122,13 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
   if (prm.sched == kSchedLocal) {
     // every CTA range holds at most tiles_per_cta * nwin units (<= kWarps * kStages)
     prm.slots = (int)(tiles_per_cta * prm.nwin);
-    smem = ring_x_offset<L>(prm.slots) + 1024 + tail_smem_bytes<PACK, NB, XM>(p.K) + LP::kBytes;
+    smem = local_smem;
   }
+  if (smem > di.smem_optin) {
+    set_error("shared memory %d exceeds the device limit %d", smem, di.smem_optin);
+    return W4A16_ERR_SHAPE;
+  }
+  prm.out_swiglu = p.out_swiglu ? 1 : 0;
   prm.pro_src = p.pro_src;
   prm.pro_gamma = p.pro_gamma;
   prm.pro_eps = p.pro_eps;

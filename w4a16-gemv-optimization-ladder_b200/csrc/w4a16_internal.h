@@ -41,6 +41,7 @@ struct GemvProblem {
   unsigned long long tp_wait_ns = 0;  // limit of each wait on another rank's flags
   bool staged = false;              // fused entry: x staged in shared memory, TMA kernel only
   bool pdl = false;                 // programmatic dependent launch (staged GEMV only)
+  bool out_swiglu = false;          // gate / up row pairs per 16-row block -> silu(g) * u (RMSNorm only)
   cudaStream_t stream = nullptr;
 };
 

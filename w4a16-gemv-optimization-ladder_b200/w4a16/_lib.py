@@ -21,6 +21,7 @@ PROLOGUE_NONE = 0
 PROLOGUE_RMSNORM = 1
 PROLOGUE_SWIGLU = 2
 LAUNCH_PDL = 1
+LAUNCH_SWIGLU_OUT = 2
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

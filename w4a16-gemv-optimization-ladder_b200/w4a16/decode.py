@@ -214,7 +214,9 @@ class W4A16LlamaDecoder:
         if self.fused and (dense or cfg.head_dim != 64):
             raise ValueError("the fused step needs int4 weights and head_dim 64")
         # the one-kernel step keeps gate and up rows interleaved by 8 (SwiGLU in the epilogue)
-        self.gu_interleaved = self.persistent
+        # the one-kernel step and the fused launches apply SwiGLU to gate / up row pairs in
+        # the gate|up epilogue
+        self.gu_interleaved = self.persistent or self.fused
         # chained launches (each kernel starts while the previous one finishes)
         self.pdl = self.fused if pdl is None else bool(pdl) and self.fused
         dev = torch.device(device)
@@ -272,6 +274,7 @@ class W4A16LlamaDecoder:
         self.h = torch.empty(H, dtype=torch.float32, device=dev)
         self.qkv = torch.empty(cfg.qkv_rows, dtype=torch.float16, device=dev)
         self.gu = torch.empty(2 * I, dtype=torch.float16, device=dev)
+        self.act = torch.empty(I, dtype=torch.float16, device=dev)  # silu(gate) * up (fused step)
         self.attn = torch.empty(cfg.heads * D, dtype=torch.float16, device=dev)
         # two split-K workspaces, alternated so that overlapping neighbours never share one
         self.ws = [K.new_workspace(dev), K.new_workspace(dev)] if self.fused else None
@@ -355,9 +358,9 @@ class W4A16LlamaDecoder:
                                heads=cfg.heads, kv_heads=cfg.kv_heads, out=self.attn, pdl=pdl)
             K.gemv_staged(o.packed, o.scale, self.attn, group=G, bias=self.h, out=self.h, pdl=pdl,
                           workspace=ws[1])
-            K.gemv_rmsnorm(gu.packed, gu.scale, self.h, L["norm_mlp"], cfg.eps, group=G, out=self.gu,
-                           pdl=pdl, workspace=ws[0])
-            K.gemv_swiglu(down.packed, down.scale, self.gu, group=G, bias=self.h, out=self.h, pdl=pdl,
+            K.gemv_rmsnorm(gu.packed, gu.scale, self.h, L["norm_mlp"], cfg.eps, group=G, out=self.act,
+                           pdl=pdl, workspace=ws[0], swiglu_out=True)
+            K.gemv_staged(down.packed, down.scale, self.act, group=G, bias=self.h, out=self.h, pdl=pdl,
                           workspace=ws[1])
         head = self.lm_head
         K.gemv_rmsnorm(head.packed, head.scale, self.h, self.norm_final, cfg.eps, group=G, out=self.logits,

@@ -145,17 +145,20 @@ def gemv(packed, scale, x, *, group=0, packing="interleaved", bias=None, out_dty
 
 
 def _fused(prologue, packed, scale, src, gamma, eps, group, bias, out, out_dtype, split_k, pdl,
-           workspace):
+           workspace, swiglu_out=False):
     _check_packed(packed)
     rows, cols = packed.shape[0], packed.shape[1] * 2
     dev = packed.device
     _need(group in (0, GROUP), f"group must be 0 or {GROUP}")
     _need(isinstance(scale, torch.Tensor) and scale.device == dev and scale.dtype in _SCALE_DTYPES
           and scale.is_contiguous(), "scale must be a contiguous float32/float16 CUDA tensor")
+    if swiglu_out:
+        _need(rows % 16 == 0 and bias is None, "swiglu_out needs rows % 16 == 0 and no bias")
+    n_out = rows // 2 if swiglu_out else rows
     if out is None:
-        out = torch.empty(rows, dtype=out_dtype, device=dev)
-    _need(out.device == dev and out.dtype in _OUT_DTYPES and tuple(out.shape) == (rows,)
-          and out.is_contiguous(), "out must be a contiguous fp32/fp16 [rows] tensor")
+        out = torch.empty(n_out, dtype=out_dtype, device=dev)
+    _need(out.device == dev and out.dtype in _OUT_DTYPES and tuple(out.shape) == (n_out,)
+          and out.is_contiguous(), f"out must be a contiguous fp32/fp16 [{n_out}] tensor")
     if bias is not None:
         _need(bias.device == dev and bias.dtype == torch.float32 and tuple(bias.shape) == (rows,)
               and bias.is_contiguous(), "bias must be a contiguous float32 [rows] tensor")
@@ -169,7 +172,8 @@ def _fused(prologue, packed, scale, src, gamma, eps, group, bias, out, out_dtype
         status = _lib.lib().w4a16_gemv_fused(
             _ptr(packed), _ptr(scale), _SCALE_DTYPES[scale.dtype], group, prologue, _ptr(src),
             _ptr(gamma), float(eps), rows, cols, _ptr(out), _OUT_DTYPES[out.dtype], _ptr(bias),
-            _ptr(ws), ws.numel() if ws is not None else 0, _lib.LAUNCH_PDL if pdl else 0,
+            _ptr(ws), ws.numel() if ws is not None else 0,
+            (_lib.LAUNCH_PDL if pdl else 0) | (_lib.LAUNCH_SWIGLU_OUT if swiglu_out else 0),
             _stream(dev))
     _lib.check(status, "w4a16_gemv_fused")
     return out
@@ -195,16 +199,19 @@ def gemv_staged(packed, scale, x, *, group=0, bias=None, out=None, out_dtype=tor
 
 
 def gemv_rmsnorm(packed, scale, h, gamma, eps=1e-5, *, group=0, bias=None, out=None,
-                 out_dtype=torch.float32, split_k=True, pdl=False, workspace=None):
+                 out_dtype=torch.float32, split_k=True, pdl=False, workspace=None, swiglu_out=False):
     """W @ fp16(h * rsqrt(mean(h^2) + eps) * gamma) (+ bias): RMSNorm fused into the GEMV.
 
-    h, gamma: fp32 [cols] on the weights' device.  out may alias bias (in-place residual)."""
+    h, gamma: fp32 [cols] on the weights' device.  out may alias bias (in-place residual).
+    swiglu_out: W holds gate / up row pairs in blocks of 16 (interleave_gate_up's layout:
+    8 gate rows, then their 8 up rows) and out[rows // 2] = silu(gate) * up of the fp32
+    sums, the activation of a Llama MLP applied in the epilogue (no bias)."""
     cols = packed.shape[1] * 2
     for name, t in (("h", h), ("gamma", gamma)):
         _need(isinstance(t, torch.Tensor) and t.device == packed.device and t.dtype == torch.float32
               and tuple(t.shape) == (cols,) and t.is_contiguous(), f"{name} must be fp32 [{cols}]")
     return _fused(_lib.PROLOGUE_RMSNORM, packed, scale, h, gamma, eps, group, bias, out, out_dtype,
-                  split_k, pdl, workspace)
+                  split_k, pdl, workspace, swiglu_out)
 
 
 def gemv_swiglu(packed, scale, gate_up, *, group=0, bias=None, out=None, out_dtype=torch.float32,
