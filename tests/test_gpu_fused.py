@@ -237,7 +237,10 @@ def test_decode_attention_position_out_of_range():
 
 # ------------------------------------------------------------ chained launches
 
-@pytest.mark.parametrize("rows,cols", [(2048, 2048), (3000, 4096)])
+# (2048, 2048) and (1000, 1536): two windows per CTA, so 4 warps share each window (slabs
+# split between them; 1536 columns leave two parts of the second window empty);
+# (3000, 4096): 4-8 windows per CTA and a partial last tile
+@pytest.mark.parametrize("rows,cols", [(2048, 2048), (3000, 4096), (1000, 1536), (64, 512)])
 def test_gemv_staged_matches_oracle(rows, cols):
     packed, scale, pk, s = _weights(rows, cols, 128, seed=rows + 5)
     x = torch.randn(cols, device="cuda").half()

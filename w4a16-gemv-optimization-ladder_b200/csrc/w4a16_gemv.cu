@@ -227,6 +227,14 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS && WAR
   const long long U = local ? (long long)ntl * nwin : p.units;
   const int T = local ? WARPS : p.nwarps;
   const bool active = gw < T;
+  // kSchedLocal with few windows per CTA (the decode geometry, group-128, one staged vector):
+  // fsplit warps share each window, warp w summing slabs [(w % fsplit) * 4 / fsplit, ...) of
+  // window w / fsplit of the CTA range, so a CTA of two windows keeps 8 warps busy, not 2.
+  constexpr bool kCanSplit = WARPS == W4A16_DECODE_WARPS && GS != 0 && NB == 1 && XS && SLABS == 4 && !TP;
+  const int fsplit = kCanSplit && local && !swo ? (U * 4 <= WARPS ? 4 : U * 2 <= WARPS ? 2 : 1) : 1;
+  const bool split = fsplit > 1;
+  const int sgrp = warp / fsplit, spart = warp - sgrp * fsplit;  // window in the range, part
+  const bool sgrp_ok = sgrp < U;
   const bool dyn = p.sched == kSchedDynamic;
   unsigned* next_tile = p.counters + kNextTileCounter;
   auto pull_tile = [&]() -> int {  // dynamic scheduling: the next unclaimed tile
@@ -241,6 +249,9 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS && WAR
   } else if (p.sched == kSchedStreamK) {
     u0 = (long long)gw * U / T;
     u1 = (long long)(gw + 1) * U / T;
+  } else if (local && split) {  // the group's first warp issues its window's copy
+    u0 = (long long)tb0 * nwin + sgrp;
+    u1 = u0 + (spart == 0 && sgrp_ok ? 1 : 0);
   } else if (local) {  // units counted from the CTA's first tile
     u0 = (long long)tb0 * nwin + (long long)gw * U / T;
     u1 = (long long)tb0 * nwin + (long long)(gw + 1) * U / T;
@@ -256,7 +267,7 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS && WAR
   // A warp's ring is STAGES consecutive slots from slot0; under kSchedLocal its units
   // (count <= STAGES, no wrap) take the slots of their places in the CTA range.
   // (gw * U / T is u0 - tb0 * nwin under kSchedLocal; it does not wait for a tile claim)
-  const int slot0 = local ? (int)((long long)gw * U / T) : warp * STAGES;
+  const int slot0 = local ? (split ? (sgrp_ok ? sgrp : 0) : (int)((long long)gw * U / T)) : warp * STAGES;
   const uint32_t wring = base + (uint32_t)(slot0 * L::kWStride);
   const uint32_t sring = base + (uint32_t)(nslots * L::kWStride + slot0 * L::kSStride);
   const uint32_t bar0 = base + (uint32_t)(nslots * (L::kWStride + L::kSStride) + slot0 * 8);
@@ -568,6 +579,49 @@ __global__ void __launch_bounds__(WARPS * 32, WARPS == W4A16_DECODE_WARPS && WAR
       }
     }
   };
+
+  if (kCanSplit && split) {
+    // The window's mbarrier was initialised by its issuing warp before the staging barrier.
+    float tot[RT][NH][4], acc[RT][2][NH][4];
+#pragma unroll
+    for (int rt = 0; rt < RT; ++rt)
+#pragma unroll
+      for (int h = 0; h < NH; ++h)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tot[rt][h][i] = acc[rt][0][h][i] = acc[rt][1][h][i] = 0.f;
+    if (sgrp_ok) {
+      if (!mbar_wait_bounded(bar0, 0u, kStageWaitLimitNs)) {
+        record_device_error(kDevErrStageTimeout);
+        if (spart == 0) mbar_wait_bounded(bar0, 0u, kDrainWaitLimitNs);  // its copy may still land
+      } else {
+        const int win = (int)(sgrp % nwin);
+        const int s0 = win * SLABS;
+        const int sa = spart * (SLABS / fsplit), sb = min(sa + SLABS / fsplit, ks - s0);
+        if (sb > sa)
+          consume_window<false, XS, PACK, GS, ST, NB, RT, SLABS, FOLD, FOLDLO>(
+              wring, sring, xs, corr, sb, s0 * kSlabCols, p.x, p.K, p.M, g, t, lo, acc, tot, sa);
+      }
+      float* lp = lpart + ((long long)sgrp * fsplit + spart) * kRows;  // [window][part][rows]
+      if (t == 0) {
+#pragma unroll
+        for (int rt = 0; rt < RT; ++rt) {
+          lp[rt * 16 + g] = tot[rt][0][0];
+          lp[rt * 16 + g + 8] = tot[rt][0][2];
+        }
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < ntl * kRows; i += blockDim.x) {  // windows and parts in order
+      const int tl = i / kRows, rl = i - tl * kRows;
+      const int r = (tb0 + tl) * kRows + rl;
+      if (r >= p.N) continue;
+      float v = 0.f;
+      for (int w = 0; w < nwin * fsplit; ++w) v += lpart[((long long)tl * nwin * fsplit + w) * kRows + rl];
+      if (p.bias) v += __ldcg(p.bias + r);
+      store_out(r, r, v);
+    }
+    return;
+  }
 
   if (!active && !local) {
     tp_warp_done();

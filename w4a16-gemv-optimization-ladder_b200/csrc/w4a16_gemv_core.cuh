@@ -79,7 +79,7 @@ __device__ __forceinline__ uint4 load_x(const __half* x, int K, int M, int g, in
   return make_uint4(0u, 0u, 0u, 0u);
 }
 
-// One window of one warp: nslab (== SLABS when FULL) slabs of RT*16 rows.
+// One window of one warp: slabs [sl_first, nslab) (all SLABS when FULL) of RT*16 rows.
 // Shared-memory copy of a single activation vector, ordered so that the B fragment
 // of (128-column group G, chunk j, thread t) is 16 bytes at ((G*4 + j)*4 + t)*16: the
 // four threads of a group read 64 contiguous bytes, one conflict-free wavefront.
@@ -123,7 +123,8 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
                                                const __half* xg, int xk, int xm, int g, int t,
                                                const LaneOffsets& lo,
                                                float (&acc)[RT][2][BatchCfg<NB>::kHalves][4],
-                                               float (&tot)[RT][BatchCfg<NB>::kHalves][4]) {
+                                               float (&tot)[RT][BatchCfg<NB>::kHalves][4],
+                                               int sl_first = 0) {
   // activation fragments of this window: 16 bytes at xwin + ((sl*2 + gh)*4 + j)*64
   const uint32_t xwin = xs + lo.x + (uint32_t)(kcol0 >> 7) * 256u;
   constexpr int NH = BatchCfg<NB>::kHalves;
@@ -133,7 +134,7 @@ __device__ __forceinline__ void consume_window(uint32_t wbase, uint32_t sbase, u
   static_assert(!FOLDLO || (FOLD && GS), "FOLDLO: group-128 folded decode only");
 #pragma unroll
   for (int sl = 0; sl < SLABS; ++sl) {
-    if (FULL || sl < nslab) {
+    if (FULL || (sl >= sl_first && sl < nslab)) {  // slabs [sl_first, nslab) unless FULL
       const int kcol = kcol0 + sl * kSlabCols;
       float cinit[2] = {0.f, 0.f};
       if (FOLD && !ROWFOLD) {
