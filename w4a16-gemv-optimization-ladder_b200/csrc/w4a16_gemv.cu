@@ -54,6 +54,9 @@
 #ifndef W4A16_DECODE_WARPS  // warps of the decode-step geometry (two CTAs per SM)
 #define W4A16_DECODE_WARPS 8
 #endif
+#ifndef W4A16_DECODE_CTAS_PER_SM  // decode geometry: CTA-local ranges per SM (1: leave room for the next kernel)
+#define W4A16_DECODE_CTAS_PER_SM 1
+#endif
 #ifndef W4A16_TMA_STAGES
 #define W4A16_TMA_STAGES 2
 #endif
@@ -1156,7 +1159,8 @@ int launch_tma(const GemvProblem& p, const __half* x, int M, void* y, const Devi
                        p.workspace_bytes >= need && aligned(p.workspace, 256);
   // kSchedLocal when every CTA's share of whole tiles fits its warps' rings at once
   using LP = LocalPlan<kWarps, kStages, kTileRows>;
-  const int g_local = prm.ntiles < di.sms ? prm.ntiles : di.sms;
+  const int local_ctas = di.sms * (GEO == kGeoDecode ? W4A16_DECODE_CTAS_PER_SM : 1);
+  const int g_local = prm.ntiles < local_ctas ? prm.ntiles : local_ctas;
   const long long tiles_per_cta = (prm.ntiles + g_local - 1) / (g_local > 0 ? g_local : 1);
   const bool local_fit = g_local > 0 && tiles_per_cta * prm.nwin <= LP::kUnits;
   const int local_smem = local_fit ? ring_x_offset<L>((int)(tiles_per_cta * prm.nwin)) + 1024 +
@@ -1230,7 +1234,8 @@ bool local_fits(const GemvProblem& p, const DeviceInfo& di) {
   using G = Geometry<GEO>;
   const long long ntiles = (p.N + G::kTile - 1) / G::kTile;
   const long long nwin = (p.K / kSlabCols + kSlabs - 1) / kSlabs;
-  const long long g_local = ntiles < di.sms ? ntiles : di.sms;
+  const long long ctas = (long long)di.sms * (GEO == kGeoDecode ? W4A16_DECODE_CTAS_PER_SM : 1);
+  const long long g_local = ntiles < ctas ? ntiles : ctas;
   return p.split_k != 1 && g_local > 0 && (ntiles + g_local - 1) / g_local * nwin <= (long long)G::kW * G::kS;
 }
 
