@@ -162,7 +162,10 @@ int w4a16_gemv_fused(const uint8_t* packed, const void* scale, int scale_dtype, 
  *   out[h] = softmax(q_h . k_cache[kvh(h)][0..p] / 8) @ v_cache[kvh(h)][0..p]   (fp16 [heads*64])
  * qkv = fp16 [(heads + 2*kv_heads) * 64] laid out q | k | v; head_dim must be 64 and
  * heads / kv_heads <= 32.  Positions are split over `splits` CTAs per kv head whose
- * fp32 partial softmaxes are combined by the last one; scratch is a zero-filled device
+ * fp32 partial softmaxes are combined: with 2..16 splits and <= 8 query heads per kv
+ * head, by the first CTA of a thread-block cluster (one per kv head) through distributed
+ * shared memory, when the device can co-schedule such a cluster; otherwise by the last CTA
+ * to finish, through scratch and a per-kv-head counter.  scratch is a zero-filled device
  * buffer of w4a16_decode_attention_scratch_bytes(heads, kv_heads, splits) bytes that the
  * kernel leaves zeroed.  A position outside [0, max_len) writes nothing to the caches and
  * NaN to out.  Calls sharing a scratch buffer must be ordered on one stream.  flags: 0 or

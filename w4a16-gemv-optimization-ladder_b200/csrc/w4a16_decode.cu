@@ -14,6 +14,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "w4a16_device.cuh"
 #include "w4a16_internal.h"
 
@@ -47,7 +49,23 @@ __device__ __forceinline__ void rope_pair(float& a, float& b, const float* cos_r
   b = rb;
 }
 
-template <int MAXT>
+// Thread-block cluster helpers (the CL variant of k_decode_attention: one cluster per kv head).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// A float of CTA `rank`'s shared memory at the offset of `local` in this CTA's.
+__device__ __forceinline__ float ld_cluster_f32(const float* local, unsigned rank) {
+  uint32_t a = (uint32_t)__cvta_generic_to_shared(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
+// CL: the kv head's splits form one thread-block cluster; each CTA leaves its partial
+// softmaxes in its own shared memory and split 0 combines them through distributed shared
+// memory between two cluster barriers (no global round trips, fence or counter).
+template <int MAXT, bool CL>
 __global__ void __launch_bounds__(MAXT) k_decode_attention(const __half* qkv, const float* __restrict__ cos_t,
                                    const float* __restrict__ sin_t, const long long* __restrict__ pos_p,
                                    __half* k_cache, __half* v_cache, __half* __restrict__ out,
@@ -213,8 +231,40 @@ __global__ void __launch_bounds__(MAXT) k_decode_attention(const __half* qkv, co
     }
   }
 
-  // publish (m, l, o) for (head, split); the last split of this kv head combines
   constexpr int kPart = kHeadDim + 2;
+  if constexpr (CL) {
+    // Every CTA of the cluster reaches both barriers (the only early return, a bad
+    // position, is taken by all of them before either).
+    float* cp = sm + (group + 2) * kHeadDim;  // [group][kPart]: this CTA's partials
+    float* mine = cp + warp * kPart;
+    if (lane == 0) {
+      mine[0] = m;
+      mine[1] = l;
+    }
+    mine[2 + 2 * lane] = o.x;
+    mine[3 + 2 * lane] = o.y;
+    cluster_sync_all();  // every split's partials are in place
+    if (split == 0) {
+      // lane s holds split s's max and weight; each lane gathers its two dims of every
+      // split's output, summed in split order (splits <= 32)
+      const float ms = lane < splits ? ld_cluster_f32(mine, (unsigned)lane) : -INFINITY;
+      const float M = warp_max(ms);
+      const float w = lane < splits && ms != -INFINITY ? __expf(ms - M) : 0.f;
+      const float lw = lane < splits ? ld_cluster_f32(mine + 1, (unsigned)lane) * w : 0.f;
+      float L = 0.f;
+      float2 a = make_float2(0.f, 0.f);
+      for (int u = 0; u < splits; ++u) {
+        const float wu = __shfl_sync(0xffffffffu, w, u);
+        L += __shfl_sync(0xffffffffu, lw, u);
+        a.x = fmaf(ld_cluster_f32(mine + 2 + 2 * lane, (unsigned)u), wu, a.x);
+        a.y = fmaf(ld_cluster_f32(mine + 3 + 2 * lane, (unsigned)u), wu, a.y);
+      }
+      reinterpret_cast<__half2*>(out + head * kHeadDim)[lane] = __floats2half2_rn(a.x / L, a.y / L);
+    }
+    cluster_sync_all();  // no CTA exits while split 0 reads its shared memory
+    return;
+  }
+  // publish (m, l, o) for (head, split); the last split of this kv head combines
   float* part = scratch + ((size_t)head * splits + split) * kPart;
   if (lane == 0) {
     part[0] = m;
@@ -446,9 +496,55 @@ int launch_decode_attention(const void* qkv, const float* cos_t, const float* si
     return W4A16_OK;
   }
   const size_t smem = (size_t)(group + 2) * kHeadDim * 4;
+  // One thread-block cluster per kv head (2..16 splits, up to 8 query heads): the splits
+  // combine through distributed shared memory.  Used when the device can co-schedule such a
+  // cluster (checked once per device and cluster size), else the global-memory combine.
+  if (group <= 8 && splits >= 2 && splits <= 16) {
+    static std::atomic<uint64_t> tried[17], usable[17];
+    int dev = 0;
+    (void)cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    auto ck = k_decode_attention<256, true>;
+    const size_t csm = smem + (size_t)group * (kHeadDim + 2) * 4;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kv_heads * splits);
+    cfg.blockDim = dim3(32 * group);
+    cfg.dynamicSmemBytes = csm;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    if (!(tried[splits].load(std::memory_order_acquire) & bit)) {
+      bool ok = cudaFuncSetAttribute(ck, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+      int nclusters = 0;
+      cfg.numAttrs = 1;
+      ok = ok && cudaOccupancyMaxActiveClusters(&nclusters, ck, &cfg) == cudaSuccess && nclusters > 0;
+      (void)cudaGetLastError();
+      if (ok) usable[splits].fetch_or(bit, std::memory_order_acq_rel);
+      tried[splits].fetch_or(bit, std::memory_order_acq_rel);
+    }
+    if (usable[splits].load(std::memory_order_acquire) & bit) {
+      cfg.numAttrs = pdl ? 2 : 1;
+      cudaError_t e = cudaLaunchKernelEx(&cfg, ck, static_cast<const __half*>(qkv), cos_t, sin_t, pos,
+                                         static_cast<__half*>(k_cache), static_cast<__half*>(v_cache),
+                                         static_cast<__half*>(out), static_cast<float*>(scratch), heads,
+                                         kv_heads, max_len, splits, 1.0f / sqrtf((float)head_dim));
+      (void)cudaGetLastError();
+      if (e != cudaSuccess) {
+        set_error("k_decode_attention (cluster) launch failed: %s", cudaGetErrorString(e));
+        return W4A16_ERR_CUDA;
+      }
+      return W4A16_OK;
+    }
+  }
   // up to 8 query heads per kv head (256 threads) the prefetch keeps its registers;
   // larger groups run with the register cap of 1024-thread blocks
-  auto kernel = group <= 8 ? k_decode_attention<256> : k_decode_attention<1024>;
+  auto kernel = group <= 8 ? k_decode_attention<256, false> : k_decode_attention<1024, false>;
   cudaError_t e = launch_maybe_pdl(
       kernel, dim3(kv_heads * splits), dim3(32 * group), smem, stream, pdl,
       static_cast<const __half*>(qkv), cos_t, sin_t, pos, static_cast<__half*>(k_cache),
